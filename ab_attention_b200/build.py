@@ -1,0 +1,83 @@
+"""Build libabx.so (the sm_100a kernels + C ABI) in-tree with nvcc.
+
+The library is loaded by ab_attention_b200._lib through ctypes. Every kernel is
+compiled for sm_100a only; the IBCS/SIP sources use --use_fast_math because
+the reference kernels they must match bit-for-bit are built that way
+(reference setup.py:12-15).
+
+Usage: python -m ab_attention_b200.build [--force] [--jobs N]
+"""
+from __future__ import annotations
+
+import argparse
+import concurrent.futures as futures
+import os
+import shutil
+import subprocess
+import sys
+from pathlib import Path
+
+PKG = Path(__file__).resolve().parent
+ROOT = PKG.parent
+CSRC = PKG / "csrc"
+BUILD = PKG / "_build"
+LIB = PKG / "libabx.so"
+SOURCES = ("ibcs.cu", "sip.cu", "prefill.cu", "capi.cu")
+HEADERS = ("common.cuh", "ibcs.cuh")
+ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
+NVCC_FLAGS = [
+    "-O3", "-std=c++17", "-lineinfo", "--use_fast_math", "-Xcompiler", "-fPIC",
+    "--expt-relaxed-constexpr", "-I", str(ROOT / "include"), "-I", str(CSRC),
+    *ARCH,
+]
+
+
+def nvcc() -> str:
+    cuda = os.environ.get("CUDA_HOME", "/usr/local/cuda")
+    path = Path(cuda) / "bin" / "nvcc"
+    return str(path) if path.exists() else (shutil.which("nvcc") or "nvcc")
+
+
+def _stale(target: Path, deps) -> bool:
+    if not target.exists():
+        return True
+    t = target.stat().st_mtime
+    return any(Path(d).stat().st_mtime > t for d in deps)
+
+
+def build(force: bool = False, jobs: int = 4, verbose: bool = False) -> Path:
+    BUILD.mkdir(exist_ok=True)
+    headers = [CSRC / h for h in HEADERS] + [ROOT / "include" / "abx.h"]
+    objects = []
+    commands = []
+    for src in SOURCES:
+        obj = BUILD / (Path(src).stem + ".o")
+        objects.append(obj)
+        if force or _stale(obj, [CSRC / src, *headers]):
+            commands.append([nvcc(), *NVCC_FLAGS, "-c", str(CSRC / src), "-o", str(obj)])
+
+    def run(cmd):
+        if verbose:
+            print(" ".join(cmd), flush=True)
+        proc = subprocess.run(cmd, capture_output=True, text=True)
+        if proc.returncode != 0:
+            raise RuntimeError(f"nvcc failed:\n{' '.join(cmd)}\n{proc.stdout}\n{proc.stderr}")
+        return proc.stderr
+
+    with futures.ThreadPoolExecutor(max_workers=max(1, jobs)) as pool:
+        for out in pool.map(run, commands):
+            if verbose and out:
+                print(out)
+    if force or commands or _stale(LIB, objects):
+        run([nvcc(), "-shared", *ARCH, "-o", str(LIB), *map(str, objects)])
+    return LIB
+
+
+if __name__ == "__main__":
+    parser = argparse.ArgumentParser()
+    parser.add_argument("--force", action="store_true")
+    parser.add_argument("--jobs", type=int, default=4)
+    parser.add_argument("-v", "--verbose", action="store_true")
+    args = parser.parse_args()
+    print(build(args.force, args.jobs, args.verbose))
+    sys.exit(0)

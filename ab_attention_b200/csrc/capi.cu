@@ -1,0 +1,300 @@
+// extern "C" boundary of libabx (declared in include/abx.h).
+//
+// Validates every argument on the host, lays out the caller-owned workspace,
+// and launches the kernels on the caller's stream. No allocation, no host
+// synchronisation (except abx_device_status, which reads the error word).
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+
+#include "common.cuh"
+#include "ibcs.cuh"
+
+namespace abx {
+
+__device__ int g_device_error = 0;
+
+int* device_error_word() {
+    void* ptr = nullptr;
+    if (cudaGetSymbolAddress(&ptr, g_device_error) != cudaSuccess) return nullptr;
+    return static_cast<int*>(ptr);
+}
+
+}  // namespace abx
+
+namespace {
+
+thread_local char g_last_error[512] = "";
+
+int fail(int status, const char* fmt, ...) {
+    va_list args;
+    va_start(args, fmt);
+    vsnprintf(g_last_error, sizeof(g_last_error), fmt, args);
+    va_end(args);
+    return status;
+}
+
+int check_cuda(cudaError_t err, const char* what) {
+    if (err == cudaSuccess) return ABX_OK;
+    return fail(ABX_ERR_CUDA, "%s: %s", what, cudaGetErrorString(err));
+}
+
+constexpr size_t kAlign = 256;
+size_t align_up(size_t x) { return (x + kAlign - 1) / kAlign * kAlign; }
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+// Workspace of the IBCS stages for (bh, seq).
+struct IbcsLayout {
+    int64_t qb, rows, fine, ld;
+    size_t scaled, populations, pooled, lse, lse_max, lse_den, total;
+};
+
+IbcsLayout ibcs_layout(int64_t bh, int64_t seq) {
+    IbcsLayout l{};
+    l.qb = abx::ceil_div(seq, abx::kQueryBlock);
+    l.rows = bh * l.qb;
+    l.fine = seq / abx::kKv4;
+    l.ld = (l.fine + 7) / 8 * 8;
+    size_t off = 0;
+    l.scaled = off;
+    off = align_up(off + static_cast<size_t>(l.rows) * abx::kCentroids * abx::kHeadDim * 2);
+    l.populations = off;
+    off = align_up(off + static_cast<size_t>(l.rows) * abx::kCentroids * 4);
+    l.pooled = off;
+    off = align_up(off + static_cast<size_t>(bh) * l.fine * abx::kReps * abx::kHeadDim * 2);
+    l.lse = off;
+    off = align_up(off + static_cast<size_t>(l.rows) * abx::kCentroids * l.ld * 2);
+    l.lse_max = off;
+    off = align_up(off + static_cast<size_t>(l.rows) * abx::kCentroids * 4);
+    l.lse_den = off;
+    off = align_up(off + static_cast<size_t>(l.rows) * abx::kCentroids * 4);
+    l.total = off;
+    return l;
+}
+
+int check_qk_shape(int64_t bh, int64_t seq) {
+    if (bh <= 0) return fail(ABX_ERR_INVALID_ARGUMENT, "batch*heads must be positive (got %lld)", (long long)bh);
+    if (seq <= 0 || seq % abx::kKv4 != 0)
+        return fail(ABX_ERR_INVALID_ARGUMENT, "sequence length must be a positive multiple of 4 (got %lld)", (long long)seq);
+    const int64_t fine = seq / abx::kKv4;
+    if (fine > abx::kMaxFineBlocks)
+        return fail(ABX_ERR_UNSUPPORTED, "KV4 block count must be in [1, 32768] (got %lld)", (long long)fine);
+    if (bh * abx::ceil_div(seq, abx::kQueryBlock) > 0x7fffffffLL)
+        return fail(ABX_ERR_UNSUPPORTED, "too many query blocks");
+    return ABX_OK;
+}
+
+int check_sip_shape(int64_t rows, int64_t population, int64_t samples) {
+    if (rows <= 0) return fail(ABX_ERR_INVALID_ARGUMENT, "row count must be positive");
+    if (samples <= 0 || samples >= population)
+        return fail(ABX_ERR_INVALID_ARGUMENT, "sample count must be inside the population (0 < %lld < %lld)",
+                    (long long)samples, (long long)population);
+    if (population > 0x7fffffffLL) return fail(ABX_ERR_UNSUPPORTED, "population too large");
+    const size_t need = abx::sip_smem_bytes(population);
+    const int limit = abx::sip_smem_limit();
+    if (limit <= 0 || need > static_cast<size_t>(limit))
+        return fail(ABX_ERR_UNSUPPORTED, "population exceeds single-block shared memory capacity (%zu > %d bytes)",
+                    need, limit);
+    return ABX_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int abx_version(void) { return 1; }
+
+const char* abx_status_string(int status) {
+    switch (status) {
+        case ABX_OK: return "ok";
+        case ABX_ERR_INVALID_ARGUMENT: return "invalid argument";
+        case ABX_ERR_UNSUPPORTED: return "unsupported shape";
+        case ABX_ERR_WORKSPACE: return "workspace too small or misaligned";
+        case ABX_ERR_CUDA: return "CUDA error";
+        case ABX_ERR_DEVICE_TIMEOUT: return "device-side wait timed out";
+        default: return "unknown status";
+    }
+}
+
+const char* abx_last_error(void) { return g_last_error; }
+
+int abx_device_status(abx_stream_t stream, int clear, int* status_out) {
+    if (status_out == nullptr) return fail(ABX_ERR_INVALID_ARGUMENT, "status_out is null");
+    int value = 0;
+    int st = check_cuda(cudaMemcpyFromSymbolAsync(&value, abx::g_device_error, sizeof(int), 0,
+                                                  cudaMemcpyDeviceToHost, stream),
+                        "read device status");
+    if (st) return st;
+    st = check_cuda(cudaStreamSynchronize(stream), "synchronize");
+    if (st) return st;
+    if (clear) {
+        const int zero = 0;
+        st = check_cuda(cudaMemcpyToSymbolAsync(abx::g_device_error, &zero, sizeof(int), 0,
+                                                cudaMemcpyHostToDevice, stream),
+                        "clear device status");
+        if (st) return st;
+        st = check_cuda(cudaStreamSynchronize(stream), "synchronize");
+        if (st) return st;
+    }
+    *status_out = value;
+    return ABX_OK;
+}
+
+int abx_ibcs_cluster(const void* q, int64_t bh, int64_t seq, void* centroids, void* scaled_centroids,
+                     float* populations, int32_t* assignments, abx_stream_t stream) {
+    if (int st = check_qk_shape(bh, seq)) return st;
+    if (q == nullptr || populations == nullptr)
+        return fail(ABX_ERR_INVALID_ARGUMENT, "q and populations must be non-null");
+    if (!aligned16(q) || (centroids && !aligned16(centroids)) || (scaled_centroids && !aligned16(scaled_centroids)))
+        return fail(ABX_ERR_INVALID_ARGUMENT, "q and centroid buffers must be 16-byte aligned");
+    return check_cuda(abx::launch_cluster(static_cast<const abx::bf16*>(q), bh, seq,
+                                          static_cast<abx::bf16*>(centroids),
+                                          static_cast<abx::bf16*>(scaled_centroids), populations,
+                                          assignments, stream),
+                      "cluster launch");
+}
+
+int abx_ibcs_pool(const void* k, int64_t bh, int64_t seq, void* pooled, abx_stream_t stream) {
+    if (int st = check_qk_shape(bh, seq)) return st;
+    if (k == nullptr || pooled == nullptr) return fail(ABX_ERR_INVALID_ARGUMENT, "k and pooled must be non-null");
+    if (!aligned16(k) || !aligned16(pooled)) return fail(ABX_ERR_INVALID_ARGUMENT, "k and pooled must be 16-byte aligned");
+    return check_cuda(abx::launch_pool(static_cast<const abx::bf16*>(k), bh, seq, static_cast<abx::bf16*>(pooled), stream),
+                      "pool launch");
+}
+
+int abx_ibcs_lse(const void* scaled_centroids, const void* pooled, int64_t bh, int64_t qb,
+                 int64_t fine_blocks, uint16_t* lse, float* lse_max, float* lse_den, abx_stream_t stream) {
+    if (bh <= 0 || qb <= 0 || fine_blocks <= 0 || fine_blocks > abx::kMaxFineBlocks)
+        return fail(ABX_ERR_INVALID_ARGUMENT, "bad IBCS LSE shape");
+    if (!scaled_centroids || !pooled || !lse || !lse_max || !lse_den)
+        return fail(ABX_ERR_INVALID_ARGUMENT, "IBCS LSE buffers must be non-null");
+    if (!aligned16(scaled_centroids) || !aligned16(pooled) || !aligned16(lse))
+        return fail(ABX_ERR_INVALID_ARGUMENT, "IBCS LSE buffers must be 16-byte aligned");
+    return check_cuda(abx::launch_lse(static_cast<const abx::bf16*>(scaled_centroids),
+                                      static_cast<const abx::bf16*>(pooled), bh, qb, fine_blocks,
+                                      fine_blocks, reinterpret_cast<half*>(lse), lse_max, lse_den, stream),
+                      "lse launch");
+}
+
+int abx_ibcs_mix(const uint16_t* lse, const float* populations, const float* lse_max, const float* lse_den,
+                 int64_t rows, int64_t fine_blocks, float* scores, abx_stream_t stream) {
+    if (rows <= 0 || fine_blocks <= 0) return fail(ABX_ERR_INVALID_ARGUMENT, "bad IBCS mix shape");
+    if (!lse || !populations || !lse_max || !lse_den || !scores)
+        return fail(ABX_ERR_INVALID_ARGUMENT, "IBCS mix buffers must be non-null");
+    return check_cuda(abx::launch_mix(reinterpret_cast<const half*>(lse), fine_blocks, populations, lse_max,
+                                      lse_den, rows, fine_blocks, scores, stream),
+                      "mix launch");
+}
+
+int abx_ibcs_workspace_size(int64_t bh, int64_t seq, size_t* bytes) {
+    if (bytes == nullptr) return fail(ABX_ERR_INVALID_ARGUMENT, "bytes is null");
+    if (int st = check_qk_shape(bh, seq)) return st;
+    *bytes = ibcs_layout(bh, seq).total;
+    return ABX_OK;
+}
+
+static int run_ibcs_front(const void* q, const void* k, int64_t bh, int64_t seq, void* workspace,
+                          size_t workspace_bytes, const IbcsLayout& l, cudaStream_t stream) {
+    if (workspace == nullptr || (reinterpret_cast<uintptr_t>(workspace) % kAlign) != 0)
+        return fail(ABX_ERR_WORKSPACE, "workspace must be non-null and 256-byte aligned");
+    if (workspace_bytes < l.total)
+        return fail(ABX_ERR_WORKSPACE, "workspace too small (%zu < %zu bytes)", workspace_bytes, l.total);
+    if (!q || !k || !aligned16(q) || !aligned16(k))
+        return fail(ABX_ERR_INVALID_ARGUMENT, "q and k must be non-null and 16-byte aligned");
+    char* ws = static_cast<char*>(workspace);
+    auto* scaled = reinterpret_cast<abx::bf16*>(ws + l.scaled);
+    auto* pops = reinterpret_cast<float*>(ws + l.populations);
+    auto* pooled = reinterpret_cast<abx::bf16*>(ws + l.pooled);
+    auto* lse = reinterpret_cast<half*>(ws + l.lse);
+    auto* mx = reinterpret_cast<float*>(ws + l.lse_max);
+    auto* den = reinterpret_cast<float*>(ws + l.lse_den);
+    if (int st = check_cuda(abx::launch_cluster(static_cast<const abx::bf16*>(q), bh, seq, nullptr, scaled,
+                                                pops, nullptr, stream), "cluster launch"))
+        return st;
+    if (int st = check_cuda(abx::launch_pool(static_cast<const abx::bf16*>(k), bh, seq, pooled, stream),
+                            "pool launch"))
+        return st;
+    return check_cuda(abx::launch_lse(scaled, pooled, bh, l.qb, l.fine, l.ld, lse, mx, den, stream), "lse launch");
+}
+
+int abx_ibcs_scores(const void* q, const void* k, int64_t bh, int64_t seq, float* scores, void* workspace,
+                    size_t workspace_bytes, abx_stream_t stream) {
+    if (int st = check_qk_shape(bh, seq)) return st;
+    if (scores == nullptr) return fail(ABX_ERR_INVALID_ARGUMENT, "scores is null");
+    const IbcsLayout l = ibcs_layout(bh, seq);
+    if (int st = run_ibcs_front(q, k, bh, seq, workspace, workspace_bytes, l, stream)) return st;
+    char* ws = static_cast<char*>(workspace);
+    return check_cuda(abx::launch_mix(reinterpret_cast<const half*>(ws + l.lse), l.ld,
+                                      reinterpret_cast<const float*>(ws + l.populations),
+                                      reinterpret_cast<const float*>(ws + l.lse_max),
+                                      reinterpret_cast<const float*>(ws + l.lse_den), l.rows, l.fine, scores,
+                                      stream),
+                      "mix launch");
+}
+
+int abx_sip(const float* scores, const float* offsets, int64_t rows, int64_t population, int32_t* ids,
+            float* log_weights, int64_t samples, abx_stream_t stream) {
+    if (int st = check_sip_shape(rows, population, samples)) return st;
+    if (!scores || !offsets || !ids || !log_weights)
+        return fail(ABX_ERR_INVALID_ARGUMENT, "SIP buffers must be non-null");
+    return check_cuda(abx::launch_sip(scores, offsets, rows, population, ids, log_weights, samples, stream),
+                      "sip launch");
+}
+
+int abx_build_plan(const void* q, const void* k, int64_t bh, int64_t seq, const float* offsets, int64_t samples,
+                   int32_t* ids, float* log_weights, void* workspace, size_t workspace_bytes,
+                   abx_stream_t stream) {
+    if (int st = check_qk_shape(bh, seq)) return st;
+    const IbcsLayout l = ibcs_layout(bh, seq);
+    if (int st = check_sip_shape(l.rows, l.fine, samples)) return st;
+    if (!offsets || !ids || !log_weights) return fail(ABX_ERR_INVALID_ARGUMENT, "plan buffers must be non-null");
+    if (int st = run_ibcs_front(q, k, bh, seq, workspace, workspace_bytes, l, stream)) return st;
+    char* ws = static_cast<char*>(workspace);
+    return check_cuda(abx::launch_mix_sip(reinterpret_cast<const half*>(ws + l.lse), l.ld,
+                                          reinterpret_cast<const float*>(ws + l.populations),
+                                          reinterpret_cast<const float*>(ws + l.lse_max),
+                                          reinterpret_cast<const float*>(ws + l.lse_den), offsets, l.rows, l.fine,
+                                          ids, log_weights, samples, stream),
+                      "mix+sip launch");
+}
+
+int abx_sparse_prefill(const void* q, const void* k, const void* v, int64_t bh, int64_t seq, const int32_t* ids,
+                       const float* log_weights, int64_t samples, const void* text_k, const void* text_v,
+                       int64_t text_tokens, void* o, float* lse, abx_stream_t stream) {
+    if (int st = check_qk_shape(bh, seq)) return st;
+    if (!q || !k || !v || !o) return fail(ABX_ERR_INVALID_ARGUMENT, "q, k, v and o must be non-null");
+    if (!aligned16(q) || !aligned16(k) || !aligned16(v) || !aligned16(o))
+        return fail(ABX_ERR_INVALID_ARGUMENT, "q, k, v and o must be 16-byte aligned");
+    if (samples < 0 || samples > seq / abx::kKv4)
+        return fail(ABX_ERR_INVALID_ARGUMENT, "samples must be in [0, seq/4] (got %lld)", (long long)samples);
+    if (samples > 0 && (ids == nullptr || log_weights == nullptr))
+        return fail(ABX_ERR_INVALID_ARGUMENT, "ids and log_weights must be non-null");
+    if (text_tokens < 0 || text_tokens % abx::kKv4 != 0)
+        return fail(ABX_ERR_INVALID_ARGUMENT, "text token count must be a non-negative multiple of 4");
+    if (text_tokens > 0 && (!text_k || !text_v || !aligned16(text_k) || !aligned16(text_v)))
+        return fail(ABX_ERR_INVALID_ARGUMENT, "text_k/text_v must be non-null and 16-byte aligned");
+    if (samples + text_tokens / abx::kKv4 <= 0)
+        return fail(ABX_ERR_INVALID_ARGUMENT, "every row needs at least one key block");
+    return check_cuda(abx::launch_prefill(static_cast<const abx::bf16*>(q), static_cast<const abx::bf16*>(k),
+                                          static_cast<const abx::bf16*>(v), bh, seq, ids, log_weights, samples,
+                                          static_cast<const abx::bf16*>(text_k),
+                                          static_cast<const abx::bf16*>(text_v), text_tokens,
+                                          static_cast<abx::bf16*>(o), lse, stream),
+                      "prefill launch");
+}
+
+int abx_dense_prefill(const void* q, const void* k, const void* v, int64_t bh, int64_t seq, void* o, float* lse,
+                      abx_stream_t stream) {
+    if (int st = check_qk_shape(bh, seq)) return st;
+    if (!q || !k || !v || !o) return fail(ABX_ERR_INVALID_ARGUMENT, "q, k, v and o must be non-null");
+    if (!aligned16(q) || !aligned16(k) || !aligned16(v) || !aligned16(o))
+        return fail(ABX_ERR_INVALID_ARGUMENT, "q, k, v and o must be 16-byte aligned");
+    return check_cuda(abx::launch_prefill(static_cast<const abx::bf16*>(q), static_cast<const abx::bf16*>(k),
+                                          static_cast<const abx::bf16*>(v), bh, seq, nullptr, nullptr,
+                                          seq / abx::kKv4, nullptr, nullptr, 0, static_cast<abx::bf16*>(o), lse,
+                                          stream),
+                      "prefill launch");
+}
+
+}  // extern "C"

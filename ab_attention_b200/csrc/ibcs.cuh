@@ -1,0 +1,36 @@
+// Launchers of the IBCS, SIP and prefill kernels (called by the C ABI layer,
+// which validates every argument first).
+#pragma once
+
+#include "common.cuh"
+
+namespace abx {
+
+cudaError_t launch_cluster(const bf16* q, int64_t bh, int64_t seq, bf16* centroids, bf16* scaled,
+                           float* populations, int32_t* assignments, cudaStream_t stream);
+cudaError_t launch_pool(const bf16* k, int64_t bh, int64_t seq, bf16* pooled, cudaStream_t stream);
+size_t lse_smem_bytes();
+cudaError_t launch_lse(const bf16* scaled, const bf16* pooled, int64_t bh, int64_t qb,
+                       int64_t fine_blocks, int64_t ld, half* lse, float* lse_max, float* lse_den,
+                       cudaStream_t stream);
+cudaError_t launch_mix(const half* lse, int64_t ld, const float* populations, const float* lse_max,
+                       const float* lse_den, int64_t rows, int64_t fine_blocks, float* scores,
+                       cudaStream_t stream);
+
+// SIP over a dense score array (csrc/sip.cu) or fused with the IBCS mixture.
+size_t sip_smem_bytes(int64_t population);
+int sip_smem_limit();
+cudaError_t launch_sip(const float* scores, const float* offsets, int64_t rows, int64_t population,
+                       int32_t* ids, float* log_weights, int64_t samples, cudaStream_t stream);
+cudaError_t launch_mix_sip(const half* lse, int64_t ld, const float* populations,
+                           const float* lse_max, const float* lse_den, const float* offsets,
+                           int64_t rows, int64_t population, int32_t* ids, float* log_weights,
+                           int64_t samples, cudaStream_t stream);
+
+// Sparse / dense prefill.
+cudaError_t launch_prefill(const bf16* q, const bf16* k, const bf16* v, int64_t bh, int64_t seq,
+                           const int32_t* ids, const float* log_weights, int64_t samples,
+                           const bf16* text_k, const bf16* text_v, int64_t text_tokens, bf16* o,
+                           float* lse, cudaStream_t stream);
+
+}  // namespace abx

@@ -1,0 +1,186 @@
+"""Tensor-level wrappers over the libabx C ABI (the custom-op layer).
+
+These replace the reference's pybind module `ab_attention._C` (csrc/bindings.cpp:3-8)
+and FlashInfer adapter (ab_attention/flashinfer_backend.py:164-242). Every op
+runs on the tensors' device and the current CUDA stream, allocates its outputs
+with the torch caching allocator, and raises on any nonzero status. There is
+no CPU implementation.
+"""
+from __future__ import annotations
+
+import ctypes
+import math
+
+import torch
+
+from . import _lib
+
+HEAD_DIM = 128
+QUERY_BLOCK = 128
+KV4 = 4
+CENTROIDS = 8
+
+
+def _as3(x: torch.Tensor) -> torch.Tensor:
+    """[B,H,N,D] or [BH,N,D] -> contiguous [BH,N,D]."""
+    if x.ndim == 4:
+        x = x.reshape(x.shape[0] * x.shape[1], x.shape[2], x.shape[3])
+    return x.contiguous()
+
+
+def _check_qk(q: torch.Tensor, k: torch.Tensor) -> None:
+    _lib.require_cuda(q, k)
+    if q.device != k.device:
+        raise RuntimeError("q and k must use the same CUDA device")
+    if q.dtype != torch.bfloat16 or k.dtype != torch.bfloat16:
+        raise RuntimeError("IBCS requires bfloat16 q/k")
+    if q.shape[-1] != HEAD_DIM:
+        raise RuntimeError("IBCS requires head_dim=128")
+
+
+def workspace_size(batch_heads: int, tokens: int) -> int:
+    out = ctypes.c_size_t(0)
+    lib = _lib.load()
+    _lib.check(lib.abx_ibcs_workspace_size(batch_heads, tokens, ctypes.byref(out)), "abx_ibcs_workspace_size")
+    return out.value
+
+
+def _workspace(batch_heads: int, tokens: int, device) -> torch.Tensor:
+    return torch.empty(workspace_size(batch_heads, tokens), dtype=torch.uint8, device=device)
+
+
+# ---- IBCS stages (parity) ------------------------------------------------------
+
+def cluster(q: torch.Tensor):
+    """q [BH,S,128] bf16 -> (centroids bf16 [rows,8,128], scaled bf16 [rows,8,128],
+    populations f32 [rows,8], assignments i32 [rows,128])."""
+    q3 = _as3(q)
+    _check_qk(q3, q3)
+    bh, seq, _ = q3.shape
+    rows = bh * math.ceil(seq / QUERY_BLOCK)
+    cent = torch.empty((rows, CENTROIDS, HEAD_DIM), dtype=torch.bfloat16, device=q3.device)
+    scaled = torch.empty_like(cent)
+    pops = torch.empty((rows, CENTROIDS), dtype=torch.float32, device=q3.device)
+    assign = torch.empty((rows, QUERY_BLOCK), dtype=torch.int32, device=q3.device)
+    lib = _lib.load()
+    with torch.cuda.device(q3.device):
+        _lib.check(lib.abx_ibcs_cluster(_lib.ptr(q3), bh, seq, _lib.ptr(cent), _lib.ptr(scaled), _lib.ptr(pops),
+                                        _lib.ptr(assign), _lib.stream_of(q3)), "abx_ibcs_cluster")
+    return cent, scaled, pops, assign
+
+
+def pool(k: torch.Tensor) -> torch.Tensor:
+    """k [BH,S,128] bf16 -> pooled key representatives bf16 [BH,S/4,2,128]."""
+    k3 = _as3(k)
+    _check_qk(k3, k3)
+    bh, seq, _ = k3.shape
+    out = torch.empty((bh, seq // KV4, 2, HEAD_DIM), dtype=torch.bfloat16, device=k3.device)
+    lib = _lib.load()
+    with torch.cuda.device(k3.device):
+        _lib.check(lib.abx_ibcs_pool(_lib.ptr(k3), bh, seq, _lib.ptr(out), _lib.stream_of(k3)), "abx_ibcs_pool")
+    return out
+
+
+def lse(scaled: torch.Tensor, pooled: torch.Tensor, q_blocks: int):
+    """scaled centroids [BH*qb,8,128], pooled [BH,F,2,128] -> (lse fp16 [rows,8,F], max f32 [rows,8], den f32 [rows,8])."""
+    bh, fine = pooled.shape[0], pooled.shape[1]
+    rows = bh * q_blocks
+    out = torch.empty((rows, CENTROIDS, fine), dtype=torch.float16, device=pooled.device)
+    mx = torch.empty((rows, CENTROIDS), dtype=torch.float32, device=pooled.device)
+    den = torch.empty_like(mx)
+    lib = _lib.load()
+    with torch.cuda.device(pooled.device):
+        _lib.check(lib.abx_ibcs_lse(_lib.ptr(scaled.contiguous()), _lib.ptr(pooled.contiguous()), bh, q_blocks, fine,
+                                    _lib.ptr(out), _lib.ptr(mx), _lib.ptr(den), _lib.stream_of(pooled)),
+                   "abx_ibcs_lse")
+    return out, mx, den
+
+
+def mix(lse_: torch.Tensor, populations: torch.Tensor, lse_max: torch.Tensor, lse_den: torch.Tensor):
+    """Population-weighted mixture -> scores f32 [rows, F]."""
+    rows, _, fine = lse_.shape
+    out = torch.empty((rows, fine), dtype=torch.float32, device=lse_.device)
+    lib = _lib.load()
+    pops = populations.to(torch.float32).contiguous()
+    with torch.cuda.device(lse_.device):
+        _lib.check(lib.abx_ibcs_mix(_lib.ptr(lse_.contiguous()), _lib.ptr(pops), _lib.ptr(lse_max.contiguous()),
+                                    _lib.ptr(lse_den.contiguous()), rows, fine, _lib.ptr(out),
+                                    _lib.stream_of(lse_)), "abx_ibcs_mix")
+    return out
+
+
+# ---- reference native ops ----------------------------------------------------------
+
+def ibcs(q: torch.Tensor, k: torch.Tensor) -> torch.Tensor:
+    """`_C.ibcs(q, k)` (csrc/ibcs.cu:549-617): q/k bf16 [B,H,S,128] -> scores f32 [B*H*qb, S/4]."""
+    _check_qk(q, k)
+    if q.shape != k.shape or q.ndim != 4:
+        raise RuntimeError("q and k must have matching [batch, heads, tokens, 128] shapes")
+    q3, k3 = _as3(q), _as3(k)
+    bh, seq, _ = q3.shape
+    rows = bh * math.ceil(seq / QUERY_BLOCK)
+    scores = torch.empty((rows, seq // KV4), dtype=torch.float32, device=q.device)
+    lib = _lib.load()
+    with torch.cuda.device(q.device):
+        ws = _workspace(bh, seq, q.device)
+        _lib.check(lib.abx_ibcs_scores(_lib.ptr(q3), _lib.ptr(k3), bh, seq, _lib.ptr(scores), _lib.ptr(ws),
+                                       ws.numel(), _lib.stream_of(q3)), "abx_ibcs_scores")
+    return scores
+
+
+def sip(scores: torch.Tensor, offsets: torch.Tensor, ids: torch.Tensor, logs: torch.Tensor) -> None:
+    """`_C.sip(scores, offsets, ids, logs)` (csrc/sip.cu:170-199): writes ids/logs in place."""
+    _lib.require_cuda(scores, offsets, ids, logs)
+    if not (offsets.device == scores.device == ids.device == logs.device):
+        raise RuntimeError("all SIP tensors must share a CUDA device")
+    if (scores.dtype != torch.float32 or offsets.dtype != torch.float32 or ids.dtype != torch.int32
+            or logs.dtype != torch.float32):
+        raise RuntimeError("SIP requires float32 scores/offsets/weights and int32 ids")
+    if scores.ndim != 2 or offsets.ndim != 1 or ids.ndim != 2 or ids.shape != logs.shape:
+        raise RuntimeError("expected scores [rows,N], offsets [rows], ids/weights [rows,samples]")
+    if not (scores.is_contiguous() and offsets.is_contiguous() and ids.is_contiguous() and logs.is_contiguous()):
+        raise RuntimeError("SIP tensors must be contiguous")
+    if not (scores.shape[0] == offsets.shape[0] == ids.shape[0]):
+        raise RuntimeError("row counts must agree")
+    lib = _lib.load()
+    with torch.cuda.device(scores.device):
+        _lib.check(lib.abx_sip(_lib.ptr(scores), _lib.ptr(offsets), scores.shape[0], scores.shape[1], _lib.ptr(ids),
+                               _lib.ptr(logs), ids.shape[1], _lib.stream_of(scores)), "abx_sip")
+
+
+def build_plan_into(q3: torch.Tensor, k3: torch.Tensor, offsets: torch.Tensor, ids: torch.Tensor,
+                    logw: torch.Tensor, workspace: torch.Tensor) -> None:
+    """Fused IBCS + SIP for contiguous [BH,S,128] q/k into [rows, samples] ids/logw."""
+    bh, seq, _ = q3.shape
+    lib = _lib.load()
+    with torch.cuda.device(q3.device):
+        _lib.check(lib.abx_build_plan(_lib.ptr(q3), _lib.ptr(k3), bh, seq, _lib.ptr(offsets), ids.shape[-1],
+                                      _lib.ptr(ids), _lib.ptr(logw), _lib.ptr(workspace), workspace.numel(),
+                                      _lib.stream_of(q3)), "abx_build_plan")
+
+
+def sparse_prefill(q3, k3, v3, ids, logw, *, text_k=None, text_v=None, return_lse=False):
+    """HT-weighted sparse prefill over [BH,S,128] bf16 q/k/v; ids/logw [rows, samples]."""
+    bh, seq, _ = q3.shape
+    samples = ids.shape[-1]
+    o = torch.empty_like(q3)
+    lse_ = torch.empty((bh, seq), dtype=torch.float32, device=q3.device) if return_lse else None
+    text_tokens = 0 if text_k is None else text_k.shape[1]
+    lib = _lib.load()
+    with torch.cuda.device(q3.device):
+        _lib.check(lib.abx_sparse_prefill(_lib.ptr(q3), _lib.ptr(k3), _lib.ptr(v3), bh, seq, _lib.ptr(ids),
+                                          _lib.ptr(logw), samples, _lib.ptr(text_k), _lib.ptr(text_v), text_tokens,
+                                          _lib.ptr(o), _lib.ptr(lse_), _lib.stream_of(q3)), "abx_sparse_prefill")
+    return o, lse_
+
+
+def dense_prefill(q3, k3, v3, *, return_lse=False):
+    """Dense attention through the same prefill kernel (the dense comparator)."""
+    bh, seq, _ = q3.shape
+    o = torch.empty_like(q3)
+    lse_ = torch.empty((bh, seq), dtype=torch.float32, device=q3.device) if return_lse else None
+    lib = _lib.load()
+    with torch.cuda.device(q3.device):
+        _lib.check(lib.abx_dense_prefill(_lib.ptr(q3), _lib.ptr(k3), _lib.ptr(v3), bh, seq, _lib.ptr(o),
+                                         _lib.ptr(lse_), _lib.stream_of(q3)), "abx_dense_prefill")
+    return o, lse_

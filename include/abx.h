@@ -1,0 +1,131 @@
+/*
+ * abx.h — C ABI of the B200 (sm_100a) AB-Attention sparse-attention hot path.
+ *
+ * The reference binds its kernels through a pybind11 module (`ab_attention._C`,
+ * csrc/bindings.cpp:3-8, csrc/ops.h:5-8) and runs the sparse prefill through
+ * FlashInfer (ab_attention/flashinfer_backend.py:164-242). This header is the
+ * replacement boundary: plain pointers, sizes and a cudaStream_t, no torch types.
+ *
+ * Conventions shared by every entry point:
+ *   - Tensors are dense, row-major, on the current CUDA device. `bh` is batch*heads,
+ *     `seq` the token count; q/k/v are bf16 [bh, seq, 128] (head dim fixed at 128
+ *     as in csrc/ibcs.cu:32 and flashinfer_backend.py:19).
+ *   - qb = ceil(seq/128) query blocks, F = seq/4 KV4 blocks, rows = bh*qb.
+ *   - Every call is asynchronous on `stream` and returns an abx_status; 0 is success.
+ *     The caller owns every buffer, including workspaces sized by *_workspace_size.
+ *   - bf16 / fp16 buffers are passed as `void*` / `uint16_t*` (raw 16-bit words).
+ */
+#ifndef ABX_H_
+#define ABX_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct CUstream_st* abx_stream_t; /* identical to cudaStream_t */
+
+enum abx_status {
+  ABX_OK = 0,
+  ABX_ERR_INVALID_ARGUMENT = 1, /* null pointer, bad shape or size                      */
+  ABX_ERR_UNSUPPORTED = 2,      /* shape outside a kernel limit (F > 32768, smem cap)  */
+  ABX_ERR_WORKSPACE = 3,        /* workspace missing, too small or misaligned           */
+  ABX_ERR_CUDA = 4,             /* a CUDA runtime call or kernel launch failed          */
+  ABX_ERR_DEVICE_TIMEOUT = 5    /* a bounded device-side wait gave up (see abx_device_status) */
+};
+
+/* Library identification and error text. abx_last_error() is thread-local. */
+int abx_version(void);
+const char* abx_status_string(int status);
+const char* abx_last_error(void);
+
+/* Sticky device-side error word for the current device (0 = none): set by a
+ * kernel whose bounded wait expired. Reading it synchronizes `stream`; pass
+ * clear=1 to reset it. */
+int abx_device_status(abx_stream_t stream, int clear, int* status_out);
+
+/* ---------------------------------------------------------------------------
+ * IBCS stages (parity entry points). Each mirrors one reference kernel.
+ * ------------------------------------------------------------------------- */
+
+/* cluster_queries_kernel (csrc/ibcs.cu:106-238): farthest-first 8-way clustering
+ * of each 128-query block. Outputs (any may be NULL except populations):
+ *   centroids        bf16 [rows, 8, 128]   bf16_rn(mean of members), 0 if empty
+ *   scaled_centroids bf16 [rows, 8, 128]   bf16_rn(centroid * 128^-0.5 * log2 e)
+ *                                          (the MMA operand, csrc/ibcs.cu:293-295)
+ *   populations      f32  [rows, 8]        member counts (the reference stores fp16)
+ *   assignments      i32  [rows, 128]      centroid slot per query, -1 past the end */
+int abx_ibcs_cluster(const void* q, int64_t bh, int64_t seq, void* centroids,
+                     void* scaled_centroids, float* populations, int32_t* assignments,
+                     abx_stream_t stream);
+
+/* pool_keys_kernel (csrc/ibcs.cu:244-266): two representatives per KV4 block,
+ * bf16_rn(0.5*(k[4j+2t] + k[4j+2t+1])). pooled: bf16 [bh, F, 2, 128]. */
+int abx_ibcs_pool(const void* k, int64_t bh, int64_t seq, void* pooled, abx_stream_t stream);
+
+/* ibcs_lse_kernel (csrc/ibcs.cu:370-489): per (row, centroid, KV4 block) the fp16
+ * pair log2-sum-exp of the two scaled centroid.key scores, plus each (row,
+ * centroid)'s running normalizer. lse: fp16 [rows, 8, F]; lse_max/lse_den: f32 [rows, 8]. */
+int abx_ibcs_lse(const void* scaled_centroids, const void* pooled, int64_t bh, int64_t qb,
+                 int64_t fine_blocks, uint16_t* lse, float* lse_max, float* lse_den,
+                 abx_stream_t stream);
+
+/* ibcs_scores_kernel (csrc/ibcs.cu:495-538): population-weighted mixture of the
+ * eight centroid distributions. scores: f32 [rows, F]. */
+int abx_ibcs_mix(const uint16_t* lse, const float* populations, const float* lse_max,
+                 const float* lse_den, int64_t rows, int64_t fine_blocks, float* scores,
+                 abx_stream_t stream);
+
+/* ---------------------------------------------------------------------------
+ * Replacements for the reference native ops.
+ * ------------------------------------------------------------------------- */
+
+/* Workspace for abx_ibcs_scores and abx_build_plan (bytes, 256-byte aligned base). */
+int abx_ibcs_workspace_size(int64_t bh, int64_t seq, size_t* bytes);
+
+/* `_C.ibcs(q, k) -> scores` (csrc/ibcs.cu:549-617): all four IBCS stages.
+ * scores: f32 [rows, F]. */
+int abx_ibcs_scores(const void* q, const void* k, int64_t bh, int64_t seq, float* scores,
+                    void* workspace, size_t workspace_bytes, abx_stream_t stream);
+
+/* `_C.sip(scores, offsets, ids, logs)` (csrc/sip.cu:170-199): iterative pi=1
+ * certainty then systematic sampling without replacement. scores f32 [rows,
+ * population], offsets f32 [rows] in [0,1), ids i32 [rows, samples] and
+ * log_weights f32 [rows, samples] written in place. 0 < samples < population. */
+int abx_sip(const float* scores, const float* offsets, int64_t rows, int64_t population,
+            int32_t* ids, float* log_weights, int64_t samples, abx_stream_t stream);
+
+/* build_plan's device work (ab_attention/attention.py:27-82) in one call:
+ * IBCS with the mixture fused into SIP, so the per-block scores never reach HBM.
+ * ids/log_weights: [rows, samples]. Same results as abx_ibcs_scores + abx_sip. */
+int abx_build_plan(const void* q, const void* k, int64_t bh, int64_t seq,
+                   const float* offsets, int64_t samples, int32_t* ids, float* log_weights,
+                   void* workspace, size_t workspace_bytes, abx_stream_t stream);
+
+/* ---------------------------------------------------------------------------
+ * Sparse prefill: replaces flashinfer_backend.paged_attention
+ * (ab_attention/flashinfer_backend.py:164-242) and its ABSipAttention variant (:30-58).
+ * For each row (bh, query block) the keys are the KV4 blocks ids[row, 0..samples)
+ * (local to the head), each with logit shift log_weights[row, slot] in log2 units,
+ * followed by `text_tokens` always-included keys from text_k/text_v
+ * ([bh, text_tokens, 128], shift 0; NULL when text_tokens == 0).
+ *   o   bf16 [bh, seq, 128]
+ *   lse f32  [bh, seq] base-2 log-sum-exp of the scaled logits (NULL to skip)
+ * ------------------------------------------------------------------------- */
+int abx_sparse_prefill(const void* q, const void* k, const void* v, int64_t bh, int64_t seq,
+                       const int32_t* ids, const float* log_weights, int64_t samples,
+                       const void* text_k, const void* text_v, int64_t text_tokens,
+                       void* o, float* lse, abx_stream_t stream);
+
+/* Dense attention through the same prefill kernel (every KV4 block, shift 0):
+ * the dense comparator. o / lse as above. */
+int abx_dense_prefill(const void* q, const void* k, const void* v, int64_t bh, int64_t seq,
+                      void* o, float* lse, abx_stream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* ABX_H_ */

@@ -1,0 +1,65 @@
+"""The C ABI library loads and exports every symbol include/abx.h declares;
+host-side argument validation answers without touching a GPU."""
+import ctypes
+
+import pytest
+
+from ab_attention_b200 import _lib
+
+
+def test_library_exports_every_header_symbol():
+    lib = _lib.load()
+    names = _lib.header_symbols()
+    assert len(names) >= 14
+    missing = [n for n in names if not hasattr(lib, n)]
+    assert not missing, missing
+    assert set(_lib._SIGNATURES) == set(names), "ctypes signatures out of sync with abx.h"
+
+
+def test_status_strings_and_version():
+    lib = _lib.load()
+    assert lib.abx_version() >= 1
+    assert lib.abx_status_string(0) == b"ok"
+    for code in range(1, 6):
+        assert lib.abx_status_string(code) != b"unknown status"
+
+
+@pytest.mark.parametrize("bh,seq,status", [
+    (0, 1024, 1),          # no heads
+    (2, 1026, 1),          # not a multiple of 4
+    (2, -4, 1),
+    (1, 4 * 32769, 2),     # more than 32768 KV4 blocks (csrc/ibcs.cu:567)
+])
+def test_workspace_size_rejects_bad_shapes(bh, seq, status):
+    lib = _lib.load()
+    out = ctypes.c_size_t(0)
+    assert lib.abx_ibcs_workspace_size(bh, seq, ctypes.byref(out)) == status
+    assert lib.abx_last_error()
+
+
+def test_workspace_size_layout():
+    lib = _lib.load()
+    out = ctypes.c_size_t(0)
+    bh, seq = 80, 75600
+    assert lib.abx_ibcs_workspace_size(bh, seq, ctypes.byref(out)) == 0
+    rows, fine = bh * 591, seq // 4
+    ld = (fine + 7) // 8 * 8
+    lse_bytes = rows * 8 * ld * 2
+    assert lse_bytes < out.value < lse_bytes + 2 * 1024 ** 3
+
+
+def test_compute_entry_points_validate_before_launch():
+    lib = _lib.load()
+    p = ctypes.c_void_p(16)  # never dereferenced: validation fails first
+    # samples must be inside the population
+    assert lib.abx_sip(p, p, 4, 100, p, p, 100, None) == 1
+    assert lib.abx_sip(p, p, 4, 100, p, p, 0, None) == 1
+    # null / misaligned inputs
+    assert lib.abx_ibcs_cluster(None, 1, 128, None, None, p, None, None) == 1
+    assert lib.abx_ibcs_pool(ctypes.c_void_p(18), 1, 128, p, None) == 1
+    # workspace must be present and aligned
+    assert lib.abx_ibcs_scores(p, p, 1, 1024, p, None, 0, None) in (1, 3)
+    assert lib.abx_build_plan(p, p, 1, 1024, p, 2048, p, p, None, 0, None) == 1  # samples >= F
+    # prefill: negative text tokens, samples beyond F
+    assert lib.abx_sparse_prefill(p, p, p, 1, 1024, p, p, 300, None, None, 0, p, None, None) == 1
+    assert lib.abx_sparse_prefill(p, p, p, 1, 1024, p, p, 8, None, None, -4, p, None, None) == 1
