@@ -31,6 +31,8 @@ _SIGNATURES = {
     "abx_ibcs_scores": ([_p, _p, _i64, _i64, _p, _p, ctypes.c_size_t, _p], ctypes.c_int),
     "abx_sip": ([_p, _p, _i64, _i64, _p, _p, _i64, _p], ctypes.c_int),
     "abx_build_plan": ([_p, _p, _i64, _i64, _p, _i64, _p, _p, _p, ctypes.c_size_t, _p], ctypes.c_int),
+    "abx_static_scratch_bytes": ([], ctypes.c_size_t),
+    "abx_build_plan_static": ([_p, _p, _i64, _i64, _p, _i64, _p, _p, _p], ctypes.c_int),
     "abx_sparse_prefill": ([_p, _p, _p, _i64, _i64, _p, _p, _i64, _p, _p, _i64, _p, _p, _p], ctypes.c_int),
     "abx_dense_prefill": ([_p, _p, _p, _i64, _i64, _p, _p, _p], ctypes.c_int),
 }
@@ -45,7 +47,7 @@ class AbxError(RuntimeError):
 def header_symbols() -> list[str]:
     """Every function name declared in include/abx.h."""
     text = HEADER.read_text()
-    return sorted(set(re.findall(r"^\s*(?:int|const char\*)\s+(abx_\w+)\s*\(", text, re.M)))
+    return sorted(set(re.findall(r"^\s*(?:int|size_t|const char\*)\s+(abx_\w+)\s*\(", text, re.M)))
 
 
 def load():

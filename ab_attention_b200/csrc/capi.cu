@@ -6,6 +6,7 @@
 #include <cstdarg>
 #include <cstdio>
 #include <cstring>
+#include <mutex>
 
 #include "common.cuh"
 #include "ibcs.cuh"
@@ -257,6 +258,82 @@ int abx_build_plan(const void* q, const void* k, int64_t bh, int64_t seq, const 
                                           reinterpret_cast<const float*>(ws + l.lse_den), offsets, l.rows, l.fine,
                                           ids, log_weights, samples, stream),
                       "mix+sip launch");
+}
+
+}  // extern "C"
+
+// ---------------------------------------------------------------------------
+// Allocation-free build_plan: the IBCS scratch lives in a fixed device array.
+//
+// Some callers cannot call cudaMalloc: a host process whose device memory is
+// owned by another allocator (a framework's caching pool, or a serving runtime
+// that reserves all memory up front), a plugin host that forbids allocation
+// after start-up, or a latency-critical path that cannot afford cudaMalloc's
+// implicit device synchronisation. abx_build_plan_static serves them: it needs
+// no workspace argument and allocates nothing, using the 256 MiB array below,
+// which every GPU that loads libabx holds until the process exits.
+// ---------------------------------------------------------------------------
+namespace {
+
+constexpr size_t kStaticScratchBytes = size_t(256) << 20;
+static __device__ __align__(256) unsigned char g_static_scratch[kStaticScratchBytes];
+
+std::mutex g_static_scratch_mutex;
+constexpr int kMaxDevices = 64;
+void* g_static_scratch_ptr[kMaxDevices] = {};
+
+// Device address of g_static_scratch on the current device. In host code the
+// array's name is only a host-side stand-in, so the address is looked up once
+// per device with cudaGetSymbolAddress (with that device current) and cached.
+int static_scratch(void** out) {
+    int device = -1;
+    if (int st = check_cuda(cudaGetDevice(&device), "cudaGetDevice")) return st;
+    if (device < 0 || device >= kMaxDevices) return fail(ABX_ERR_UNSUPPORTED, "device ordinal %d out of range", device);
+    std::lock_guard<std::mutex> lock(g_static_scratch_mutex);
+    if (g_static_scratch_ptr[device] == nullptr) {
+        void* ptr = nullptr;
+        if (int st = check_cuda(cudaGetSymbolAddress(&ptr, g_static_scratch), "cudaGetSymbolAddress(static scratch)"))
+            return st;
+        g_static_scratch_ptr[device] = ptr;
+    }
+    *out = g_static_scratch_ptr[device];
+    return ABX_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+size_t abx_static_scratch_bytes(void) { return kStaticScratchBytes; }
+
+int abx_build_plan_static(const void* q, const void* k, int64_t bh, int64_t seq, const float* offsets,
+                          int64_t samples, int32_t* ids, float* log_weights, abx_stream_t stream) {
+    if (int st = check_qk_shape(bh, seq)) return st;
+    const IbcsLayout one = ibcs_layout(1, seq);
+    if (one.total > kStaticScratchBytes)
+        return fail(ABX_ERR_WORKSPACE,
+                    "abx_build_plan_static: one head of %lld tokens needs %zu bytes of scratch, more than the "
+                    "fixed %zu-byte array; use abx_build_plan with a caller workspace",
+                    (long long)seq, one.total, kStaticScratchBytes);
+    if (int st = check_sip_shape(one.rows, one.fine, samples)) return st;
+    if (!q || !k || !offsets || !ids || !log_weights)
+        return fail(ABX_ERR_INVALID_ARGUMENT, "q, k, offsets, ids and log_weights must be non-null");
+    void* scratch = nullptr;
+    if (int st = static_scratch(&scratch)) return st;
+    // Heads per pass: as many as the array holds; passes run in stream order.
+    int64_t per_pass = 1;
+    while (per_pass < bh && ibcs_layout(per_pass + 1, seq).total <= kStaticScratchBytes) ++per_pass;
+    const int64_t head_elems = seq * abx::kHeadDim;
+    for (int64_t start = 0; start < bh; start += per_pass) {
+        const int64_t heads = (bh - start) < per_pass ? (bh - start) : per_pass;
+        const int64_t row0 = start * one.qb;
+        const int st = abx_build_plan(static_cast<const abx::bf16*>(q) + start * head_elems,
+                                      static_cast<const abx::bf16*>(k) + start * head_elems, heads, seq,
+                                      offsets + row0, samples, ids + row0 * samples, log_weights + row0 * samples,
+                                      scratch, kStaticScratchBytes, stream);
+        if (st) return st;
+    }
+    return ABX_OK;
 }
 
 int abx_sparse_prefill(const void* q, const void* k, const void* v, int64_t bh, int64_t seq, const int32_t* ids,

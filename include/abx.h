@@ -104,6 +104,22 @@ int abx_build_plan(const void* q, const void* k, int64_t bh, int64_t seq,
                    const float* offsets, int64_t samples, int32_t* ids, float* log_weights,
                    void* workspace, size_t workspace_bytes, abx_stream_t stream);
 
+/* abx_build_plan without a workspace argument, for callers that cannot call
+ * cudaMalloc (device memory owned by another allocator or reserved up front, or
+ * a path where cudaMalloc's implicit synchronisation is not acceptable). No
+ * counterpart in the reference. It allocates nothing: its scratch is a fixed
+ * file-scope device array of abx_static_scratch_bytes() (256 MiB) that every GPU
+ * loading libabx holds until exit, so one head of the input must fit in it
+ * (about 90k tokens); larger inputs are rejected with ABX_ERR_WORKSPACE. Heads
+ * are processed in passes that fit the array. The first call on a device looks
+ * up the array's device address (make it before any stream capture). All calls
+ * share the array: calls that overlap on the GPU (different streams, or
+ * different host threads) race, so serialise them. Results equal abx_build_plan's. */
+size_t abx_static_scratch_bytes(void);
+int abx_build_plan_static(const void* q, const void* k, int64_t bh, int64_t seq,
+                          const float* offsets, int64_t samples, int32_t* ids,
+                          float* log_weights, abx_stream_t stream);
+
 /* ---------------------------------------------------------------------------
  * Sparse prefill: replaces flashinfer_backend.paged_attention
  * (ab_attention/flashinfer_backend.py:164-242) and its ABSipAttention variant (:30-58).
