@@ -190,11 +190,17 @@ def main() -> None:
     parser.add_argument("--no-cpu-baseline", action="store_true")
     parser.add_argument("--no-dense", action="store_true")
     parser.add_argument("--no-e2e", action="store_true")
+    parser.add_argument("--bh", type=int, default=0,
+                        help="run only the first BH (batch*head) rows of the configuration (profiling)")
     args = parser.parse_args()
 
     from ab_attention_b200.synthetic import CONFIGS, make_inputs
 
     shape = CONFIGS[args.config]
+    if args.bh:
+        import dataclasses
+
+        shape = dataclasses.replace(shape, name=f"{shape.name}[bh={args.bh}]", batch=1, heads=args.bh)
     if args.impl == "reference":
         run_reference(args, shape)
         return
