@@ -46,11 +46,10 @@ constexpr uint32_t kSlabBytes = 128 * 128;       // 128 rows x 64 bf16
 constexpr uint32_t kTileBytes = 2 * kSlabBytes;  // one 128 x 128 bf16 operand tile
 constexpr int kSoftmaxWarps = 4;
 constexpr int kMmaWarp = 4;
-constexpr int kKLoadWarp = 5;  // Q, then K tiles
-constexpr int kVLoadWarp = 6;  // V tiles
-constexpr int kThreads = 7 * 32;
-constexpr uint32_t kGranuleBytes = kKv4 * kHeadDim * 2;               // 1 KB
-constexpr uint32_t kTileTxBytes = kTileGranules * kGranuleBytes;       // 32 KB per operand tile
+constexpr int kProducerWarpsPerOperand = 2;  // 1: each lane issues both slab boxes; 2: one slab per warp
+constexpr int kKLoadWarp = 5;                                         // first K warp (also loads Q)
+constexpr int kVLoadWarp = kKLoadWarp + kProducerWarpsPerOperand;     // first V warp
+constexpr int kThreads = (kVLoadWarp + kProducerWarpsPerOperand) * 32;
 
 constexpr uint32_t kTmemColumns = 512;
 constexpr uint32_t kColO = 0;
@@ -113,15 +112,20 @@ struct PrefillMaps {
     CUtensorMap tk, tv;  // text keys / values, box 64 x 4 rows
 };
 
-// First tensor-map row of granule `slot` of this row, and whether it comes from
-// the text maps. Padding slots and out-of-range ids map to an out-of-range row
-// (the TMA reads zeros there).
-__device__ __forceinline__ int64_t granule_row(const PrefillArgs& a, int64_t head, const int32_t* row_ids,
-                                               int slot, bool& text) {
+// KV4 id of granule `slot` of this row (dense: the slot itself); -1 when the
+// slot is not a sampled granule (padding or text).
+__device__ __forceinline__ int granule_id(const PrefillArgs& a, const int32_t* row_ids, int slot) {
+    if (slot >= a.samples) return -1;
+    return row_ids ? __ldg(row_ids + slot) : slot;
+}
+
+// First tensor-map row of granule `slot` (whose id was read by granule_id), and
+// whether it comes from the text maps. Padding slots and out-of-range ids map
+// to an out-of-range row (the TMA reads zeros there).
+__device__ __forceinline__ int64_t granule_row(const PrefillArgs& a, int64_t head, int slot, int id, bool& text) {
     text = false;
     if (slot >= a.granules) return a.kv_rows;
     if (slot < a.samples) {
-        const int id = row_ids ? __ldg(row_ids + slot) : slot;
         if (id < 0 || id >= a.fine_blocks) {  // never read outside the head
             raise_device_error(a.error, ABX_ERR_INVALID_ARGUMENT);
             return a.kv_rows;
@@ -130,6 +134,12 @@ __device__ __forceinline__ int64_t granule_row(const PrefillArgs& a, int64_t hea
     }
     text = true;
     return head * a.text_tokens + static_cast<int64_t>(slot - a.samples) * kKv4;
+}
+
+// Logit shift of granule `slot`: its SIP weight, 0 for text, -inf past the end.
+__device__ __forceinline__ float slot_weight(const PrefillArgs& a, const float* row_w, int slot) {
+    if (slot >= a.granules) return -INFINITY;
+    return (slot < a.samples && row_w) ? __ldg(row_w + slot) : 0.f;
 }
 
 __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const PrefillArgs args,
@@ -158,11 +168,11 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const PrefillArgs 
         *abort_flag = 0;
         tc::mbar_init(bar(kBarQFull), 1);
         for (int s = 0; s < kKStages; ++s) {
-            tc::mbar_init(bar(kBarKFull + s), 1);
+            tc::mbar_init(bar(kBarKFull + s), kProducerWarpsPerOperand);
             tc::mbar_init(bar(kBarKEmpty + s), 1);
         }
         for (int s = 0; s < kVStages; ++s) {
-            tc::mbar_init(bar(kBarVFull + s), 1);
+            tc::mbar_init(bar(kBarVFull + s), kProducerWarpsPerOperand);
             tc::mbar_init(bar(kBarVEmpty + s), 1);
         }
         for (int b = 0; b < 2; ++b) {
@@ -183,10 +193,13 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const PrefillArgs 
     tc::fence_after_sync();
     const uint32_t tmem = *tmem_slot;
 
-    if (warp == kKLoadWarp || warp == kVLoadWarp) {
-        // ---- producers: one lane per granule, two TMA boxes each ----------------------------
-        const bool is_k = warp == kKLoadWarp;
-        if (is_k && lane == 0) {
+    if (warp >= kKLoadWarp) {
+        // ---- producers: one lane per granule, one TMA box per 64-dim slab ----------------------
+        const bool is_k = warp < kVLoadWarp;
+        const int part = warp - (is_k ? kKLoadWarp : kVLoadWarp);  // which slab, when split
+        const int slab0 = kProducerWarpsPerOperand == 2 ? part : 0;
+        const int nslabs = kProducerWarpsPerOperand == 2 ? 1 : 2;
+        if (warp == kKLoadWarp && lane == 0) {
             // Q tile: two 128-row x 64-column boxes (rows past the block are never stored).
             tc::mbar_arrive_expect_tx(bar(kBarQFull), kTileBytes);
             const int32_t qy = static_cast<int32_t>(head * args.seq + token0);
@@ -200,21 +213,25 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const PrefillArgs 
         const int bar_full = is_k ? kBarKFull : kBarVFull;
         const int bar_empty = is_k ? kBarKEmpty : kBarVEmpty;
         int issued = 0;
+        int next_id = granule_id(args, row_ids, lane);  // ids are read one tile ahead
         for (int t = 0; t < tiles; ++t) {
             const int st = t % stages;
             const int use = t / stages;
+            const int slot = t * kTileGranules + lane;
+            const int id = next_id;
+            if (t + 1 < tiles) next_id = granule_id(args, row_ids, slot + kTileGranules);
             const bool free_ok =
                 use == 0 || tc::mbar_wait(bar(bar_empty + st), (use - 1) & 1, abort_flag, kWaitLimit);
             if (!__all_sync(0xffffffffu, free_ok)) break;
             issued = t + 1;
-            if (lane == 0) tc::mbar_arrive_expect_tx(bar(bar_full + st), kTileTxBytes);
+            if (lane == 0) tc::mbar_arrive_expect_tx(bar(bar_full + st), nslabs * kSlabBytes);
             __syncwarp();
             bool text;
-            const int64_t y = granule_row(args, head, row_ids, t * kTileGranules + lane, text);
+            const int64_t y = granule_row(args, head, slot, id, text);
             const CUtensorMap* map = text ? text_map : main_map;
             const uint32_t dst = ring + st * kTileBytes + lane * (kKv4 * 128);
-            tc::tma_load_2d(dst, map, 0, static_cast<int32_t>(y), bar(bar_full + st));
-            tc::tma_load_2d(dst + kSlabBytes, map, 64, static_cast<int32_t>(y), bar(bar_full + st));
+            for (int sl = slab0; sl < slab0 + nslabs; ++sl)
+                tc::tma_load_2d(dst + sl * kSlabBytes, map, 64 * sl, static_cast<int32_t>(y), bar(bar_full + st));
         }
         // Drain: every box issued above has landed before the CTA may exit (on the
         // normal path the MMA warp consumed them all and these waits return at once).
@@ -223,7 +240,7 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const PrefillArgs 
                 const int last_use = (issued - 1 - st) / stages;
                 tc::mbar_wait(bar(bar_full + st), last_use & 1, abort_flag, kWaitLimit, /*honor_abort=*/false);
             }
-            if (is_k) tc::mbar_wait(bar(kBarQFull), 0, abort_flag, kWaitLimit, /*honor_abort=*/false);
+            if (warp == kKLoadWarp) tc::mbar_wait(bar(kBarQFull), 0, abort_flag, kWaitLimit, /*honor_abort=*/false);
         }
         __syncwarp();
     } else if (warp == kMmaWarp) {
@@ -282,36 +299,50 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const PrefillArgs 
         float m_used = -INFINITY;
         float l_sum = 0.f;
         bool ok = true;
+        // Lane j holds the weight of granule j of the current tile; the next
+        // tile's weights are read one tile ahead.
+        float w_next = slot_weight(args, row_w, lane);
         for (int t = 0; t < tiles; ++t) {
             const int b = t & 1;
+            const float w_lane = w_next;
+            if (t + 1 < tiles) w_next = slot_weight(args, row_w, (t + 1) * kTileGranules + lane);
             if (!tc::mbar_wait_warp(bar(kBarSFull + b), (t >> 1) & 1, abort_flag, kWaitLimit)) {
                 ok = false;
                 break;
             }
             tc::fence_after_sync();
-            uint32_t s[4][32];
+            const uint32_t s_col = lane_base + col_s(b);
+            // Pass 1: row max of x = s * kappa + w over the tile, streaming S from TMEM
+            // 32 columns at a time (double-buffered loads, 8 independent max chains).
+            float part_max[8];
 #pragma unroll
-            for (int c = 0; c < 4; ++c) tc::tmem_ld32(lane_base + col_s(b) + 32 * c, s[c]);
-            tc::tmem_wait_ld();
+            for (int g = 0; g < 8; ++g) part_max[g] = -INFINITY;
+            {
+                uint32_t buf[2][32];
+                tc::tmem_ld32(s_col, buf[0]);
+                tc::tmem_wait_ld();
+                tc::tmem_reg_fence(buf[0]);
 #pragma unroll
-            for (int c = 0; c < 4; ++c) tc::tmem_reg_fence(s[c]);
-            // logits in place: x = s * kappa + w (w of the key's granule)
-            float tile_max = -INFINITY;
+                for (int c = 0; c < 4; ++c) {
+                    if (c + 1 < 4) tc::tmem_ld32(s_col + 32 * (c + 1), buf[(c + 1) & 1]);
 #pragma unroll
-            for (int c = 0; c < 4; ++c) {
+                    for (int g = 0; g < 8; ++g) {
+                        const float w = __shfl_sync(0xffffffffu, w_lane, c * 8 + g);
 #pragma unroll
-                for (int g = 0; g < 8; ++g) {
-                    const int slot = t * kTileGranules + c * 8 + g;
-                    float w = -INFINITY;
-                    if (slot < args.granules) w = (slot < args.samples && row_w) ? __ldg(row_w + slot) : 0.f;
-#pragma unroll
-                    for (int e = 0; e < 4; ++e) {
-                        const float v = fmaf(__uint_as_float(s[c][4 * g + e]), args.kappa, w);
-                        s[c][4 * g + e] = __float_as_uint(v);
-                        tile_max = fmaxf(tile_max, v);
+                        for (int e = 0; e < 4; ++e)
+                            part_max[g] = fmaxf(part_max[g], fmaf(__uint_as_float(buf[c & 1][4 * g + e]), args.kappa, w));
+                    }
+                    if (c + 1 < 4) {
+                        tc::tmem_wait_ld();
+                        tc::tmem_reg_fence(buf[(c + 1) & 1]);
                     }
                 }
             }
+#pragma unroll
+            for (int width = 4; width > 0; width >>= 1)
+#pragma unroll
+                for (int g = 0; g < width; ++g) part_max[g] = fmaxf(part_max[g], part_max[g + width]);
+            const float tile_max = part_max[0];
             // Lazy rescale, decided per warp (tcgen05.ld/st are warp-collective):
             // a row whose max grew by more than 2^8 moves its reference max and
             // scales its O row and sum; the other rows of the warp scale by 1.
@@ -327,34 +358,49 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const PrefillArgs 
                         break;
                     }
                     tc::fence_after_sync();
-#pragma unroll
-                    for (int c = 0; c < 4; ++c) {
-                        uint32_t o[32];
-                        tc::tmem_ld32(lane_base + kColO + 32 * c, o);
+#pragma unroll 1
+                    for (int c = 0; c < 8; ++c) {  // 16 columns at a time: S is still live in registers
+                        uint32_t o[16];
+                        tc::tmem_ld16(lane_base + kColO + 16 * c, o);
                         tc::tmem_wait_ld();
                         tc::tmem_reg_fence(o);
 #pragma unroll
-                        for (int e = 0; e < 32; ++e) o[e] = __float_as_uint(__uint_as_float(o[e]) * scale);
-                        tc::tmem_st32(lane_base + kColO + 32 * c, o);
+                        for (int e = 0; e < 16; ++e) o[e] = __float_as_uint(__uint_as_float(o[e]) * scale);
+                        tc::tmem_st16(lane_base + kColO + 16 * c, o);
                     }
                 }
                 m_used = m_new;
             }
-            // P = 2^(x - m) as bf16 pairs over the S columns.
+            // Pass 2: P = 2^(s * kappa + (w - m)) as bf16 pairs, re-reading S in
+            // 32-column chunks; chunk c's 16 packed words overwrite S columns
+            // [16c, 16c + 16), which no later chunk reads.
+            float part_sum[4] = {0.f, 0.f, 0.f, 0.f};
+            {
+                uint32_t buf[2][32];
+                tc::tmem_ld32(s_col, buf[0]);
+                tc::tmem_wait_ld();
+                tc::tmem_reg_fence(buf[0]);
 #pragma unroll
-            for (int h = 0; h < 2; ++h) {
-                uint32_t p[32];
+                for (int c = 0; c < 4; ++c) {
+                    if (c + 1 < 4) tc::tmem_ld32(s_col + 32 * (c + 1), buf[(c + 1) & 1]);
+                    uint32_t packed[16];
 #pragma unroll
-                for (int e = 0; e < 32; ++e) {
-                    const int k0 = 64 * h + 2 * e;
-                    const float p0 = exp2f(__uint_as_float(s[k0 >> 5][k0 & 31]) - m_used);
-                    const float p1 = exp2f(__uint_as_float(s[(k0 + 1) >> 5][(k0 + 1) & 31]) - m_used);
-                    l_sum += p0 + p1;
-                    __nv_bfloat162 pair = __floats2bfloat162_rn(p0, p1);
-                    p[e] = *reinterpret_cast<uint32_t*>(&pair);
+                    for (int e = 0; e < 16; ++e) {
+                        const float wm = __shfl_sync(0xffffffffu, w_lane, c * 8 + (e >> 1)) - m_used;
+                        const float p0 = exp2f(fmaf(__uint_as_float(buf[c & 1][2 * e]), args.kappa, wm));
+                        const float p1 = exp2f(fmaf(__uint_as_float(buf[c & 1][2 * e + 1]), args.kappa, wm));
+                        part_sum[e & 3] += p0 + p1;
+                        __nv_bfloat162 pair = __floats2bfloat162_rn(p0, p1);
+                        packed[e] = *reinterpret_cast<uint32_t*>(&pair);
+                    }
+                    tc::tmem_st16(s_col + 16 * c, packed);
+                    if (c + 1 < 4) {
+                        tc::tmem_wait_ld();
+                        tc::tmem_reg_fence(buf[(c + 1) & 1]);
+                    }
                 }
-                tc::tmem_st32(lane_base + col_s(b) + 32 * h, p);
             }
+            l_sum += (part_sum[0] + part_sum[1]) + (part_sum[2] + part_sum[3]);
             tc::tmem_wait_st();
             tc::fence_before_sync();
             tc::mbar_arrive(bar(kBarPFull + b));
