@@ -9,20 +9,26 @@
 // text). o = sum 2^(l-m) v / sum 2^(l-m) and lse = m + log2(sum): the HT ratio
 // estimator of softmax attention.
 //
-// One CTA per row, warp-specialised (224 threads, at most two warps per SM
-// sub-partition so the softmax warps can hold a whole 128-column S row in registers):
-//   warps 0-3  softmax: thread i owns query row i = TMEM lane i, so row max and
-//              row sum need no shuffles. Reads S from TMEM, writes P (bf16)
-//              back over S for the PV product, rescales O lazily (only when the
-//              running max grows by more than 2^8).
-//   warp  4    TMEM allocation + MMA issue (one thread): S = Q K^T (both
-//              operands in shared memory) and O += P V (P from TMEM).
-//   warp  5    gathers Q and the K tiles, warp 6 the V tiles, with TMA: one
-//              lane per KV4 granule issues two 4-row x 64-column boxes (the two
-//              64-dim slabs) that land, 128-byte swizzled, at the granule's rows
-//              of the UMMA operand tile; the stage mbarrier counts the bytes.
-//              Granules past the end load from an out-of-range row (zero fill).
-// TMEM: O in columns [0,128), S/P double buffer in [128,256) and [256,384).
+// One CTA per row, 128-key tiles, warp-specialised (16 warps):
+//   warps 0-3, 4-7  two softmax warpgroups; group g takes the tiles t with
+//              t % 2 == g, so two independent streams of dependent math share
+//              each SM sub-partition. Thread i of a group owns query row i =
+//              TMEM lane i (row max / sum need no shuffles); it streams S out of
+//              TMEM in 16-column chunks, writes P (bf16) back over S for the PV
+//              product and rescales its O lazily (only when its running max
+//              grows by more than 2^8). Group 1 hands (m, l) to group 0, which
+//              merges the two partial softmaxes into the output.
+//   warp  8    TMEM allocation + MMA issue (one thread): S(t) = Q K(t)^T with
+//              both operands in shared memory, O(t%2) += P(t) V(t) with P read
+//              from TMEM.
+//   warps 9-11 gather Q and the K tiles, warps 12-15 the V tiles, with TMA: an
+//              operand tile is 64 boxes of 4 rows x 64 columns (32 granules x
+//              two 64-dim slabs), one box per lane, landing 128-byte swizzled at
+//              the granule's rows of the UMMA operand tile; the stage mbarrier
+//              counts the bytes. Granules past the end load from an out-of-range
+//              row (zero fill).
+// TMEM: S/P double buffer in columns [0,128) and [128,256), O of group 0 in
+// [256,384), O of group 1 in [384,512).
 // Every mbarrier wait is bounded; on expiry the CTA drains its copies and MMAs,
 // frees TMEM, records ABX_ERR_DEVICE_TIMEOUT in the device error word and exits.
 #include <cuda.h>
@@ -44,22 +50,31 @@ constexpr int kKStages = 3;
 constexpr int kVStages = 2;
 constexpr uint32_t kSlabBytes = 128 * 128;       // 128 rows x 64 bf16
 constexpr uint32_t kTileBytes = 2 * kSlabBytes;  // one 128 x 128 bf16 operand tile
-constexpr int kSoftmaxWarps = 4;
-constexpr int kMmaWarp = 4;
-constexpr int kProducerWarpsPerOperand = 2;  // 1: each lane issues both slab boxes; 2: one slab per warp
-constexpr int kKLoadWarp = 5;                                         // first K warp (also loads Q)
-constexpr int kVLoadWarp = kKLoadWarp + kProducerWarpsPerOperand;     // first V warp
-constexpr int kThreads = (kVLoadWarp + kProducerWarpsPerOperand) * 32;
+constexpr int kSoftmaxGroups = 2;
+constexpr int kMmaWarp = 8;
+// Gather warps per operand. An operand tile is 64 TMA boxes (32 granules x two
+// 64-dim slabs, box b = granule b/2, slab b%2); gather warp p of P issues boxes
+// p, p+P, p+2P, ... one per lane. (A TMA request costs the issuing warp tens of
+// cycles per active lane, so the requests are spread over several warps.)
+constexpr int kKGatherWarps = 3;
+constexpr int kVGatherWarps = 4;
+constexpr int kBoxesPerTile = 2 * kTileGranules;
+constexpr uint32_t kBoxBytes = kKv4 * 128;
+constexpr int kKLoadWarp = kMmaWarp + 1;                // first K warp (also loads Q)
+constexpr int kVLoadWarp = kKLoadWarp + kKGatherWarps;  // first V warp
+constexpr int kThreads = (kVLoadWarp + kVGatherWarps) * 32;
+constexpr int kChunk = 16;                              // TMEM columns per softmax step
 
 constexpr uint32_t kTmemColumns = 512;
-constexpr uint32_t kColO = 0;
-__device__ __forceinline__ constexpr uint32_t col_s(int b) { return 128u + 128u * static_cast<uint32_t>(b); }
+__device__ __forceinline__ constexpr uint32_t col_s(int b) { return 128u * static_cast<uint32_t>(b); }
+__device__ __forceinline__ constexpr uint32_t col_o(int g) { return 256u + 128u * static_cast<uint32_t>(g); }
 
 // shared memory map (offsets from a 1024-byte aligned base)
 constexpr uint32_t kOffQ = 0;
 constexpr uint32_t kOffK = kOffQ + kTileBytes;
 constexpr uint32_t kOffV = kOffK + kKStages * kTileBytes;
-constexpr uint32_t kOffBar = kOffV + kVStages * kTileBytes;
+constexpr uint32_t kOffMerge = kOffV + kVStages * kTileBytes;  // group 1's (m, l) per row
+constexpr uint32_t kOffBar = kOffMerge + 2 * 128 * 4;
 // barrier slots (8 bytes each)
 constexpr int kBarQFull = 0;
 constexpr int kBarKFull = 1;                      // kKStages
@@ -68,9 +83,10 @@ constexpr int kBarVFull = kBarKEmpty + kKStages;  // kVStages
 constexpr int kBarVEmpty = kBarVFull + kVStages;  // kVStages
 constexpr int kBarSFull = kBarVEmpty + kVStages;  // 2
 constexpr int kBarPFull = kBarSFull + 2;          // 2
-constexpr int kBarPv = kBarPFull + 2;
-constexpr int kBarOFinal = kBarPv + 1;
-constexpr int kBarDrain = kBarOFinal + 1;
+constexpr int kBarPv = kBarPFull + 2;             // 2 (one per O accumulator)
+constexpr int kBarOFinal = kBarPv + 2;
+constexpr int kBarMerge = kBarOFinal + 1;
+constexpr int kBarDrain = kBarMerge + 1;
 constexpr int kNumBars = kBarDrain + 1;
 constexpr uint32_t kOffTmemSlot = kOffBar + kNumBars * 8;
 constexpr uint32_t kOffAbort = kOffTmemSlot + 4;
@@ -106,10 +122,11 @@ struct PrefillArgs {
 };
 
 // Tensor maps over [rows, 128] bf16 with 64-column boxes and 128-byte swizzle.
+// Gather boxes are one granule (4 rows x 64 columns): index [operand][source]
+// with operand 0 = K, 1 = V; source 0 = the head's tokens, 1 = text tokens.
 struct PrefillMaps {
-    CUtensorMap q;       // box 64 x 128 rows
-    CUtensorMap k, v;    // box 64 x 4 rows (one granule)
-    CUtensorMap tk, tv;  // text keys / values, box 64 x 4 rows
+    CUtensorMap q;  // box 64 x 128 rows
+    CUtensorMap kv[2][2];
 };
 
 // KV4 id of granule `slot` of this row (dense: the slot itself); -1 when the
@@ -151,6 +168,8 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const PrefillArgs 
     auto bar = [&](int i) { return base + kOffBar + 8u * i; };
     volatile int* abort_flag = reinterpret_cast<volatile int*>(gbase + kOffAbort);
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(gbase + kOffTmemSlot);
+    float* merge_m = reinterpret_cast<float*>(gbase + kOffMerge);
+    float* merge_l = merge_m + 128;
 
     const int tid = threadIdx.x;
     const int warp = tid >> 5;
@@ -168,19 +187,20 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const PrefillArgs 
         *abort_flag = 0;
         tc::mbar_init(bar(kBarQFull), 1);
         for (int s = 0; s < kKStages; ++s) {
-            tc::mbar_init(bar(kBarKFull + s), kProducerWarpsPerOperand);
+            tc::mbar_init(bar(kBarKFull + s), kKGatherWarps);
             tc::mbar_init(bar(kBarKEmpty + s), 1);
         }
         for (int s = 0; s < kVStages; ++s) {
-            tc::mbar_init(bar(kBarVFull + s), kProducerWarpsPerOperand);
+            tc::mbar_init(bar(kBarVFull + s), kVGatherWarps);
             tc::mbar_init(bar(kBarVEmpty + s), 1);
         }
         for (int b = 0; b < 2; ++b) {
             tc::mbar_init(bar(kBarSFull + b), 1);
-            tc::mbar_init(bar(kBarPFull + b), kSoftmaxWarps * 32);
+            tc::mbar_init(bar(kBarPFull + b), 128);
+            tc::mbar_init(bar(kBarPv + b), 1);
         }
-        tc::mbar_init(bar(kBarPv), 1);
         tc::mbar_init(bar(kBarOFinal), 1);
+        tc::mbar_init(bar(kBarMerge), 128);
         tc::mbar_init(bar(kBarDrain), 1);
         tc::mbar_init_fence();
     }
@@ -194,11 +214,15 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const PrefillArgs 
     const uint32_t tmem = *tmem_slot;
 
     if (warp >= kKLoadWarp) {
-        // ---- producers: one lane per granule, one TMA box per 64-dim slab ----------------------
+        // ---- producers: one TMA box per lane per operand tile --------------------------------
         const bool is_k = warp < kVLoadWarp;
-        const int part = warp - (is_k ? kKLoadWarp : kVLoadWarp);  // which slab, when split
-        const int slab0 = kProducerWarpsPerOperand == 2 ? part : 0;
-        const int nslabs = kProducerWarpsPerOperand == 2 ? 1 : 2;
+        const int part = warp - (is_k ? kKLoadWarp : kVLoadWarp);
+        const int nwarps = is_k ? kKGatherWarps : kVGatherWarps;
+        const int box = part + nwarps * lane;
+        const bool has_box = box < kBoxesPerTile;
+        const int my_granule = has_box ? box >> 1 : 0;
+        const int my_slab = box & 1;
+        const int warp_boxes = (kBoxesPerTile - part + nwarps - 1) / nwarps;
         if (warp == kKLoadWarp && lane == 0) {
             // Q tile: two 128-row x 64-column boxes (rows past the block are never stored).
             tc::mbar_arrive_expect_tx(bar(kBarQFull), kTileBytes);
@@ -206,32 +230,30 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const PrefillArgs 
             tc::tma_load_2d(base + kOffQ, &maps.q, 0, qy, bar(kBarQFull));
             tc::tma_load_2d(base + kOffQ + kSlabBytes, &maps.q, 64, qy, bar(kBarQFull));
         }
-        const CUtensorMap* main_map = is_k ? &maps.k : &maps.v;
-        const CUtensorMap* text_map = is_k ? &maps.tk : &maps.tv;
+        const int op = is_k ? 0 : 1;
         const int stages = is_k ? kKStages : kVStages;
         const uint32_t ring = base + (is_k ? kOffK : kOffV);
         const int bar_full = is_k ? kBarKFull : kBarVFull;
         const int bar_empty = is_k ? kBarKEmpty : kBarVEmpty;
         int issued = 0;
-        int next_id = granule_id(args, row_ids, lane);  // ids are read one tile ahead
+        int next_id = granule_id(args, row_ids, my_granule);  // ids are read one tile ahead
         for (int t = 0; t < tiles; ++t) {
             const int st = t % stages;
             const int use = t / stages;
-            const int slot = t * kTileGranules + lane;
+            const int slot = t * kTileGranules + my_granule;
             const int id = next_id;
             if (t + 1 < tiles) next_id = granule_id(args, row_ids, slot + kTileGranules);
             const bool free_ok =
                 use == 0 || tc::mbar_wait(bar(bar_empty + st), (use - 1) & 1, abort_flag, kWaitLimit);
             if (!__all_sync(0xffffffffu, free_ok)) break;
             issued = t + 1;
-            if (lane == 0) tc::mbar_arrive_expect_tx(bar(bar_full + st), nslabs * kSlabBytes);
+            if (lane == 0) tc::mbar_arrive_expect_tx(bar(bar_full + st), warp_boxes * kBoxBytes);
             __syncwarp();
             bool text;
             const int64_t y = granule_row(args, head, slot, id, text);
-            const CUtensorMap* map = text ? text_map : main_map;
-            const uint32_t dst = ring + st * kTileBytes + lane * (kKv4 * 128);
-            for (int sl = slab0; sl < slab0 + nslabs; ++sl)
-                tc::tma_load_2d(dst + sl * kSlabBytes, map, 64 * sl, static_cast<int32_t>(y), bar(bar_full + st));
+            const uint32_t dst = ring + st * kTileBytes + my_slab * kSlabBytes + my_granule * kBoxBytes;
+            if (has_box)
+                tc::tma_load_2d(dst, &maps.kv[op][text], 64 * my_slab, static_cast<int32_t>(y), bar(bar_full + st));
         }
         // Drain: every box issued above has landed before the CTA may exit (on the
         // normal path the MMA warp consumed them all and these waits return at once).
@@ -260,10 +282,10 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const PrefillArgs 
                     // 16 keys per step: P columns [8j, 8j+8); V rows [16j, 16j+16) (MN-major,
                     // leading offset = the second 64-dim slab, stride offset = 8-row atom).
                     const uint64_t bdesc = tc::smem_desc(v_base + j * 16 * 128, kSlabBytes, 1024, tc::kSwizzle128B);
-                    tc::mma_ts(tmem + kColO, tmem + col_s(b) + 8 * j, bdesc, kIdescPV, (u > 0 || j > 0) ? 1u : 0u);
+                    tc::mma_ts(tmem + col_o(b), tmem + col_s(b) + 8 * j, bdesc, kIdescPV, (u >= 2 || j > 0) ? 1u : 0u);
                 }
                 tc::mma_commit(bar(kBarVEmpty + vst));
-                tc::mma_commit(bar(kBarPv));
+                tc::mma_commit(bar(kBarPv + b));
                 return true;
             };
             for (int t = 0; ok && t < tiles; ++t) {
@@ -294,107 +316,100 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const PrefillArgs 
         }
         __syncwarp();
     } else {
-        // ---- softmax (thread = query row = TMEM lane) -------------------------------------------
-        const uint32_t lane_base = tmem + (static_cast<uint32_t>(warp * 32) << 16);
+        // ---- softmax group g (thread = query row = TMEM lane) ---------------------------------------
+        const int g = warp >> 2;
+        const int r = tid & 127;  // query row
+        const uint32_t lane_base = tmem + (static_cast<uint32_t>((warp & 3) * 32) << 16);
+        const uint32_t o_col = lane_base + col_o(g);
         float m_used = -INFINITY;
         float l_sum = 0.f;
         bool ok = true;
-        // Lane j holds the weight of granule j of the current tile; the next
-        // tile's weights are read one tile ahead.
-        float w_next = slot_weight(args, row_w, lane);
-        for (int t = 0; t < tiles; ++t) {
-            const int b = t & 1;
+        // Lane j holds the weight of granule j of the current tile; the group's
+        // next tile (t + 2) is read one step ahead.
+        float w_next = slot_weight(args, row_w, g * kTileGranules + lane);
+        for (int t = g; t < tiles; t += kSoftmaxGroups) {
             const float w_lane = w_next;
-            if (t + 1 < tiles) w_next = slot_weight(args, row_w, (t + 1) * kTileGranules + lane);
-            if (!tc::mbar_wait_warp(bar(kBarSFull + b), (t >> 1) & 1, abort_flag, kWaitLimit)) {
+            if (t + kSoftmaxGroups < tiles)
+                w_next = slot_weight(args, row_w, (t + kSoftmaxGroups) * kTileGranules + lane);
+            if (!tc::mbar_wait_warp(bar(kBarSFull + g), (t >> 1) & 1, abort_flag, kWaitLimit)) {
                 ok = false;
                 break;
             }
             tc::fence_after_sync();
-            const uint32_t s_col = lane_base + col_s(b);
-            // Pass 1: row max of x = s * kappa + w over the tile, streaming S from TMEM
-            // 32 columns at a time (double-buffered loads, 8 independent max chains).
-            float part_max[8];
-#pragma unroll
-            for (int g = 0; g < 8; ++g) part_max[g] = -INFINITY;
+            const uint32_t s_col = lane_base + col_s(g);
+            // Pass 1: row max of x = s * kappa + w over the tile, streaming S out of
+            // TMEM 16 columns at a time (double-buffered), 4 independent chains.
+            float part_max[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
             {
-                uint32_t buf[2][32];
-                tc::tmem_ld32(s_col, buf[0]);
+                uint32_t buf[2][kChunk];
+                tc::tmem_ld16(s_col, buf[0]);
                 tc::tmem_wait_ld();
                 tc::tmem_reg_fence(buf[0]);
 #pragma unroll
-                for (int c = 0; c < 4; ++c) {
-                    if (c + 1 < 4) tc::tmem_ld32(s_col + 32 * (c + 1), buf[(c + 1) & 1]);
+                for (int c = 0; c < kTileKeys / kChunk; ++c) {
+                    if (c + 1 < kTileKeys / kChunk) tc::tmem_ld16(s_col + kChunk * (c + 1), buf[(c + 1) & 1]);
 #pragma unroll
-                    for (int g = 0; g < 8; ++g) {
-                        const float w = __shfl_sync(0xffffffffu, w_lane, c * 8 + g);
+                    for (int q4 = 0; q4 < kChunk / 4; ++q4) {
+                        const float w = __shfl_sync(0xffffffffu, w_lane, c * (kChunk / 4) + q4);
 #pragma unroll
                         for (int e = 0; e < 4; ++e)
-                            part_max[g] = fmaxf(part_max[g], fmaf(__uint_as_float(buf[c & 1][4 * g + e]), args.kappa, w));
+                            part_max[q4] =
+                                fmaxf(part_max[q4], fmaf(__uint_as_float(buf[c & 1][4 * q4 + e]), args.kappa, w));
                     }
-                    if (c + 1 < 4) {
+                    if (c + 1 < kTileKeys / kChunk) {
                         tc::tmem_wait_ld();
                         tc::tmem_reg_fence(buf[(c + 1) & 1]);
                     }
                 }
             }
-#pragma unroll
-            for (int width = 4; width > 0; width >>= 1)
-#pragma unroll
-                for (int g = 0; g < width; ++g) part_max[g] = fmaxf(part_max[g], part_max[g + width]);
-            const float tile_max = part_max[0];
+            const float tile_max = fmaxf(fmaxf(part_max[0], part_max[1]), fmaxf(part_max[2], part_max[3]));
             // Lazy rescale, decided per warp (tcgen05.ld/st are warp-collective):
             // a row whose max grew by more than 2^8 moves its reference max and
             // scales its O row and sum; the other rows of the warp scale by 1.
+            // O(g) holds PV of the group's earlier tiles, all complete: S(t) was
+            // committed after them.
             const bool grow = tile_max > m_used + kRescaleThreshold;
             if (__any_sync(0xffffffffu, grow)) {
                 const float m_new = grow ? tile_max : m_used;
                 const float scale = grow ? exp2f(m_used - m_new) : 1.0f;
                 l_sum *= scale;
-                if (t > 0) {
-                    // O holds PV(0..t-1): wait for PV(t-1), then rescale the rows in place.
-                    if (!tc::mbar_wait_warp(bar(kBarPv), (t - 1) & 1, abort_flag, kWaitLimit)) {
-                        ok = false;
-                        break;
-                    }
-                    tc::fence_after_sync();
+                if (t >= kSoftmaxGroups) {
 #pragma unroll 1
-                    for (int c = 0; c < 8; ++c) {  // 16 columns at a time: S is still live in registers
-                        uint32_t o[16];
-                        tc::tmem_ld16(lane_base + kColO + 16 * c, o);
+                    for (int c = 0; c < 128 / kChunk; ++c) {
+                        uint32_t o[kChunk];
+                        tc::tmem_ld16(o_col + kChunk * c, o);
                         tc::tmem_wait_ld();
                         tc::tmem_reg_fence(o);
 #pragma unroll
-                        for (int e = 0; e < 16; ++e) o[e] = __float_as_uint(__uint_as_float(o[e]) * scale);
-                        tc::tmem_st16(lane_base + kColO + 16 * c, o);
+                        for (int e = 0; e < kChunk; ++e) o[e] = __float_as_uint(__uint_as_float(o[e]) * scale);
+                        tc::tmem_st16(o_col + kChunk * c, o);
                     }
                 }
                 m_used = m_new;
             }
-            // Pass 2: P = 2^(s * kappa + (w - m)) as bf16 pairs, re-reading S in
-            // 32-column chunks; chunk c's 16 packed words overwrite S columns
-            // [16c, 16c + 16), which no later chunk reads.
+            // Pass 2: P = 2^(s * kappa + (w - m)) as bf16 pairs, re-reading S; chunk c's
+            // 8 packed words overwrite S columns [8c, 8c + 8), which no later chunk reads.
             float part_sum[4] = {0.f, 0.f, 0.f, 0.f};
             {
-                uint32_t buf[2][32];
-                tc::tmem_ld32(s_col, buf[0]);
+                uint32_t buf[2][kChunk];
+                tc::tmem_ld16(s_col, buf[0]);
                 tc::tmem_wait_ld();
                 tc::tmem_reg_fence(buf[0]);
 #pragma unroll
-                for (int c = 0; c < 4; ++c) {
-                    if (c + 1 < 4) tc::tmem_ld32(s_col + 32 * (c + 1), buf[(c + 1) & 1]);
-                    uint32_t packed[16];
+                for (int c = 0; c < kTileKeys / kChunk; ++c) {
+                    if (c + 1 < kTileKeys / kChunk) tc::tmem_ld16(s_col + kChunk * (c + 1), buf[(c + 1) & 1]);
+                    uint32_t packed[kChunk / 2];
 #pragma unroll
-                    for (int e = 0; e < 16; ++e) {
-                        const float wm = __shfl_sync(0xffffffffu, w_lane, c * 8 + (e >> 1)) - m_used;
+                    for (int e = 0; e < kChunk / 2; ++e) {
+                        const float wm = __shfl_sync(0xffffffffu, w_lane, c * (kChunk / 4) + (e >> 1)) - m_used;
                         const float p0 = exp2f(fmaf(__uint_as_float(buf[c & 1][2 * e]), args.kappa, wm));
                         const float p1 = exp2f(fmaf(__uint_as_float(buf[c & 1][2 * e + 1]), args.kappa, wm));
                         part_sum[e & 3] += p0 + p1;
                         __nv_bfloat162 pair = __floats2bfloat162_rn(p0, p1);
                         packed[e] = *reinterpret_cast<uint32_t*>(&pair);
                     }
-                    tc::tmem_st16(s_col + 16 * c, packed);
-                    if (c + 1 < 4) {
+                    tc::tmem_st8(s_col + (kChunk / 2) * c, packed);
+                    if (c + 1 < kTileKeys / kChunk) {
                         tc::tmem_wait_ld();
                         tc::tmem_reg_fence(buf[(c + 1) & 1]);
                     }
@@ -403,35 +418,56 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const PrefillArgs 
             l_sum += (part_sum[0] + part_sum[1]) + (part_sum[2] + part_sum[3]);
             tc::tmem_wait_st();
             tc::fence_before_sync();
-            tc::mbar_arrive(bar(kBarPFull + b));
+            tc::mbar_arrive(bar(kBarPFull + g));
         }
-        if (ok && tc::mbar_wait_warp(bar(kBarOFinal), 0, abort_flag, kWaitLimit)) {
+        if (g == 1) {
+            // Hand this group's running max and sum to group 0 (also on abort).
+            merge_m[r] = m_used;
+            merge_l[r] = l_sum;
+            tc::mbar_arrive(bar(kBarMerge));
+        } else if (ok && tc::mbar_wait_warp(bar(kBarOFinal), 0, abort_flag, kWaitLimit) &&
+                   tc::mbar_wait_warp(bar(kBarMerge), 0, abort_flag, kWaitLimit)) {
+            // Merge the two partial softmaxes: o = (O0 2^(m0-m) + O1 2^(m1-m)) / (l0 2^(m0-m) + l1 2^(m1-m)).
             tc::fence_after_sync();
-            const int r = tid;  // query row
-            const float inv = 1.f / l_sum;
+            const float m1 = merge_m[r];
+            const float l1 = merge_l[r];
+            const bool has1 = tiles > 1;  // group 1 saw at least one tile
+            const float m = has1 ? fmaxf(m_used, m1) : m_used;
+            const float s0 = exp2f(m_used - m);
+            const float s1 = has1 ? exp2f(m1 - m) : 0.f;
+            const float l = l_sum * s0 + (has1 ? l1 * s1 : 0.f);
+            const float inv = 1.f / l;
+            const float a0 = s0 * inv;
+            const float a1 = s1 * inv;
+            const uint32_t o1_col = lane_base + col_o(1);
             bf16* out_row = args.o + (head * args.seq + token0 + r) * kHeadDim;
-#pragma unroll
-            for (int c = 0; c < 4; ++c) {
-                uint32_t o[32];
-                tc::tmem_ld32(lane_base + kColO + 32 * c, o);
+#pragma unroll 1
+            for (int c = 0; c < 128 / kChunk; ++c) {
+                uint32_t o0[kChunk], o1[kChunk];
+                tc::tmem_ld16(o_col + kChunk * c, o0);
+                if (has1) tc::tmem_ld16(o1_col + kChunk * c, o1);
                 tc::tmem_wait_ld();
-                tc::tmem_reg_fence(o);
-                if (r < n) {
+                tc::tmem_reg_fence(o0);
+                tc::tmem_reg_fence(o1);
+                uint4 packed[2];
+                uint32_t* pw = reinterpret_cast<uint32_t*>(packed);
 #pragma unroll
-                    for (int v = 0; v < 4; ++v) {
-                        uint4 packed;
-                        uint32_t* pw = reinterpret_cast<uint32_t*>(&packed);
-#pragma unroll
-                        for (int e = 0; e < 4; ++e) {
-                            __nv_bfloat162 pair = __floats2bfloat162_rn(__uint_as_float(o[8 * v + 2 * e]) * inv,
-                                                                        __uint_as_float(o[8 * v + 2 * e + 1]) * inv);
-                            pw[e] = *reinterpret_cast<uint32_t*>(&pair);
-                        }
-                        *reinterpret_cast<uint4*>(out_row + 32 * c + 8 * v) = packed;
+                for (int e = 0; e < kChunk / 2; ++e) {
+                    float v0 = __uint_as_float(o0[2 * e]) * a0;
+                    float v1 = __uint_as_float(o0[2 * e + 1]) * a0;
+                    if (has1) {
+                        v0 = fmaf(__uint_as_float(o1[2 * e]), a1, v0);
+                        v1 = fmaf(__uint_as_float(o1[2 * e + 1]), a1, v1);
                     }
+                    __nv_bfloat162 pair = __floats2bfloat162_rn(v0, v1);
+                    pw[e] = *reinterpret_cast<uint32_t*>(&pair);
+                }
+                if (r < n) {
+                    reinterpret_cast<uint4*>(out_row + kChunk * c)[0] = packed[0];
+                    reinterpret_cast<uint4*>(out_row + kChunk * c)[1] = packed[1];
                 }
             }
-            if (args.lse != nullptr && r < n) args.lse[head * args.seq + token0 + r] = m_used + log2f(l_sum);
+            if (args.lse != nullptr && r < n) args.lse[head * args.seq + token0 + r] = m + log2f(l);
         }
     }
 
@@ -502,20 +538,16 @@ cudaError_t launch_prefill(const bf16* q, const bf16* k, const bf16* v, int64_t 
     PrefillMaps maps;
     cudaError_t err;
     if ((err = encode_rows(&maps.q, q, bh * seq, 128)) != cudaSuccess) return err;
-    if ((err = encode_rows(&maps.k, k, bh * seq, kKv4)) != cudaSuccess) return err;
-    if ((err = encode_rows(&maps.v, v, bh * seq, kKv4)) != cudaSuccess) return err;
     const bool has_text = text_tokens > 0 && text_k != nullptr && text_v != nullptr;
-    if ((err = encode_rows(&maps.tk, has_text ? text_k : k, has_text ? bh * text_tokens : bh * seq, kKv4)) !=
-        cudaSuccess)
-        return err;
-    if ((err = encode_rows(&maps.tv, has_text ? text_v : v, has_text ? bh * text_tokens : bh * seq, kKv4)) !=
-        cudaSuccess)
-        return err;
+    const void* sources[2][2] = {{k, has_text ? text_k : k}, {v, has_text ? text_v : v}};
+    const int64_t rows[2] = {bh * seq, has_text ? bh * text_tokens : bh * seq};
+    for (int op = 0; op < 2; ++op)
+        for (int src = 0; src < 2; ++src)
+            if ((err = encode_rows(&maps.kv[op][src], sources[op][src], rows[src], kKv4)) != cudaSuccess) return err;
     err = cudaFuncSetAttribute(prefill_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                static_cast<int>(kSmemBytes));
     if (err != cudaSuccess) return err;
-    const int64_t rows = bh * args.qb;
-    prefill_kernel<<<static_cast<unsigned>(rows), kThreads, kSmemBytes, stream>>>(args, maps);
+    prefill_kernel<<<static_cast<unsigned>(bh * args.qb), kThreads, kSmemBytes, stream>>>(args, maps);
     return cudaGetLastError();
 }
 
