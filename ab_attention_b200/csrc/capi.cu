@@ -48,7 +48,7 @@ bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) ==
 // Workspace of the IBCS stages for (bh, seq).
 struct IbcsLayout {
     int64_t qb, rows, fine, ld;
-    size_t scaled, populations, pooled, lse, lse_max, lse_den, total;
+    size_t scaled, populations, pooled, lse, lse_max, lse_den, scores, total;
 };
 
 IbcsLayout ibcs_layout(int64_t bh, int64_t seq) {
@@ -70,6 +70,8 @@ IbcsLayout ibcs_layout(int64_t bh, int64_t seq) {
     off = align_up(off + static_cast<size_t>(l.rows) * abx::kCentroids * 4);
     l.lse_den = off;
     off = align_up(off + static_cast<size_t>(l.rows) * abx::kCentroids * 4);
+    l.scores = off;  // build_plan's block scores (abx_ibcs_scores writes the caller's array instead)
+    off = align_up(off + static_cast<size_t>(l.rows) * l.fine * 4);
     l.total = off;
     return l;
 }
@@ -252,12 +254,16 @@ int abx_build_plan(const void* q, const void* k, int64_t bh, int64_t seq, const 
     if (!offsets || !ids || !log_weights) return fail(ABX_ERR_INVALID_ARGUMENT, "plan buffers must be non-null");
     if (int st = run_ibcs_front(q, k, bh, seq, workspace, workspace_bytes, l, stream)) return st;
     char* ws = static_cast<char*>(workspace);
-    return check_cuda(abx::launch_mix_sip(reinterpret_cast<const half*>(ws + l.lse), l.ld,
-                                          reinterpret_cast<const float*>(ws + l.populations),
-                                          reinterpret_cast<const float*>(ws + l.lse_max),
-                                          reinterpret_cast<const float*>(ws + l.lse_den), offsets, l.rows, l.fine,
-                                          ids, log_weights, samples, stream),
-                      "mix+sip launch");
+    float* scores = reinterpret_cast<float*>(ws + l.scores);
+    if (int st = check_cuda(abx::launch_mix(reinterpret_cast<const half*>(ws + l.lse), l.ld,
+                                            reinterpret_cast<const float*>(ws + l.populations),
+                                            reinterpret_cast<const float*>(ws + l.lse_max),
+                                            reinterpret_cast<const float*>(ws + l.lse_den), l.rows, l.fine, scores,
+                                            stream),
+                            "mix launch"))
+        return st;
+    return check_cuda(abx::launch_sip(scores, offsets, l.rows, l.fine, ids, log_weights, samples, stream),
+                      "sip launch");
 }
 
 }  // extern "C"

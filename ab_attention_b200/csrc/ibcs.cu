@@ -397,11 +397,15 @@ __global__ __launch_bounds__(kLseThreads) void lse_kernel(
 // Population-weighted mixture (standalone; build_plan fuses it into SIP).
 // ---------------------------------------------------------------------------
 
-__global__ __launch_bounds__(256) void mix_kernel(const half* __restrict__ lse, int64_t ld,
-                                                  const float* __restrict__ populations,
-                                                  const float* __restrict__ lse_max,
-                                                  const float* __restrict__ lse_den, int fine_blocks,
-                                                  float* __restrict__ scores) {
+constexpr int kMixThreads = 256;
+constexpr int kMixPerThread = 4;  // scores per thread; all 32 fp16 loads are issued before the math
+
+// grid (rows, ceil(F / (256 * 4))): a CTA covers 1024 consecutive KV4 blocks of one row.
+__global__ __launch_bounds__(kMixThreads) void mix_kernel(const half* __restrict__ lse, int64_t ld,
+                                                          const float* __restrict__ populations,
+                                                          const float* __restrict__ lse_max,
+                                                          const float* __restrict__ lse_den, int fine_blocks,
+                                                          float* __restrict__ scores) {
     __shared__ float row_max[kCentroids];
     __shared__ float row_den[kCentroids];
     __shared__ float row_weight[kCentroids];
@@ -415,15 +419,25 @@ __global__ __launch_bounds__(256) void mix_kernel(const half* __restrict__ lse, 
     float total_weight = 0.0f;
 #pragma unroll
     for (int c = 0; c < kCentroids; ++c) total_weight += row_weight[c];
-    for (int j = threadIdx.x; j < fine_blocks; j += blockDim.x) {
+    const int j0 = blockIdx.y * (kMixThreads * kMixPerThread) + threadIdx.x;
+    const half* base = lse + row * kCentroids * ld;
+    half value[kMixPerThread][kCentroids];
+#pragma unroll
+    for (int u = 0; u < kMixPerThread; ++u) {
+        const int j = min(j0 + u * kMixThreads, fine_blocks - 1);
+#pragma unroll
+        for (int c = 0; c < kCentroids; ++c) value[u][c] = base[c * ld + j];
+    }
+#pragma unroll
+    for (int u = 0; u < kMixPerThread; ++u) {
+        const int j = j0 + u * kMixThreads;
         float score = 0.0f;
 #pragma unroll
         for (int c = 0; c < kCentroids; ++c) {
-            const float value = __half2float(lse[(row * kCentroids + c) * ld + j]);
-            const float probability = exp2f(value - row_max[c]) / row_den[c];
+            const float probability = exp2f(__half2float(value[u][c]) - row_max[c]) / row_den[c];
             score += row_weight[c] * probability;
         }
-        scores[row * fine_blocks + j] = score / total_weight;
+        if (j < fine_blocks) scores[row * fine_blocks + j] = score / total_weight;
     }
 }
 
@@ -470,8 +484,10 @@ cudaError_t launch_lse(const bf16* scaled, const bf16* pooled, int64_t bh, int64
 cudaError_t launch_mix(const half* lse, int64_t ld, const float* populations, const float* lse_max,
                        const float* lse_den, int64_t rows, int64_t fine_blocks, float* scores,
                        cudaStream_t stream) {
-    mix_kernel<<<static_cast<unsigned>(rows), 256, 0, stream>>>(
-        lse, ld, populations, lse_max, lse_den, static_cast<int>(fine_blocks), scores);
+    const dim3 grid(static_cast<unsigned>(rows),
+                    static_cast<unsigned>(ceil_div(fine_blocks, kMixThreads * kMixPerThread)));
+    mix_kernel<<<grid, kMixThreads, 0, stream>>>(lse, ld, populations, lse_max, lse_den,
+                                                 static_cast<int>(fine_blocks), scores);
     return cudaGetLastError();
 }
 

@@ -17,15 +17,11 @@ cudaError_t launch_mix(const half* lse, int64_t ld, const float* populations, co
                        const float* lse_den, int64_t rows, int64_t fine_blocks, float* scores,
                        cudaStream_t stream);
 
-// SIP over a dense score array (csrc/sip.cu) or fused with the IBCS mixture.
+// SIP over a dense score array (csrc/sip.cu).
 size_t sip_smem_bytes(int64_t population);
 int sip_smem_limit();
 cudaError_t launch_sip(const float* scores, const float* offsets, int64_t rows, int64_t population,
                        int32_t* ids, float* log_weights, int64_t samples, cudaStream_t stream);
-cudaError_t launch_mix_sip(const half* lse, int64_t ld, const float* populations,
-                           const float* lse_max, const float* lse_den, const float* offsets,
-                           int64_t rows, int64_t population, int32_t* ids, float* log_weights,
-                           int64_t samples, cudaStream_t stream);
 
 // Sparse / dense prefill.
 cudaError_t launch_prefill(const bf16* q, const bf16* k, const bf16* v, int64_t bh, int64_t seq,

@@ -8,11 +8,8 @@
 // same form so that --use_fast_math / fmad contraction produce the same
 // instructions.
 //
-// Two value sources feed it:
-//   DenseScores : scores f32 [rows, population] (replaces `_C.sip`)
-//   MixedScores : the IBCS population-weighted mixture (csrc/ibcs.cu:495-538)
-//                 evaluated in the prologue straight from the fp16 LSE scratch,
-//                 so the f32 score array never exists in HBM (build_plan path).
+// Scores come from a dense f32 [rows, population] array (the IBCS mixture of
+// build_plan, or the caller's scores for `_C.sip`).
 #include <cub/block/block_reduce.cuh>
 #include <cub/block/block_scan.cuh>
 
@@ -40,65 +37,40 @@ struct DenseScores {
     }
 };
 
-// Mixture of the eight centroid distributions, same expression as the reference
-// scores kernel: score_j = (sum_c w_c * 2^(L_cj - max_c) / den_c) / sum_c w_c.
-struct MixedScores {
-    const half* lse;
-    int64_t ld;
-    const float* populations;
-    const float* lse_max;
-    const float* lse_den;
-    float row_max[kCentroids];
-    float row_den[kCentroids];
-    float row_weight[kCentroids];
-    float total_weight;
-
-    __device__ __forceinline__ void prepare(int64_t row) {
-#pragma unroll
-        for (int c = 0; c < kCentroids; ++c) {
-            row_max[c] = lse_max[row * kCentroids + c];
-            row_den[c] = lse_den[row * kCentroids + c];
-            row_weight[c] = populations[row * kCentroids + c];
-        }
-        total_weight = 0.0f;
-#pragma unroll
-        for (int c = 0; c < kCentroids; ++c) total_weight += row_weight[c];
-    }
-    __device__ __forceinline__ float score(int64_t row, int j) const {
-        float value_sum = 0.0f;
-#pragma unroll
-        for (int c = 0; c < kCentroids; ++c) {
-            const float value = __half2float(lse[(row * kCentroids + c) * ld + j]);
-            const float probability = exp2f(value - row_max[c]) / row_den[c];
-            value_sum += row_weight[c] * probability;
-        }
-        return value_sum / total_weight;
-    }
+using Reduce = cub::BlockReduce<SumMax, kSipThreads>;
+using CountScan = cub::BlockScan<int, kSipThreads>;
+using MassScan = cub::BlockScan<double, kSipThreads>;
+union Scratch {
+    Reduce::TempStorage reduce;
+    CountScan::TempStorage count;
+    MassScan::TempStorage mass;
 };
+
+// Dynamic shared memory: the bucket prefix (doubles) then the masses (floats).
+// CUB's temporaries live at the start of the prefix region: every block
+// reduction and scan finishes before the first prefix entry is written, and
+// keeping them out of static shared memory lets two rows share an SM at the
+// Wan2.1 shape (F = 18,900).
+__host__ __device__ constexpr size_t sip_prefix_region(int64_t population) {
+    const size_t prefix = static_cast<size_t>((population + kSipBucket - 1) / kSipBucket + 1) * sizeof(double);
+    return prefix > sizeof(Scratch) ? prefix : (sizeof(Scratch) + 15) / 16 * 16;
+}
 
 template <class Source>
 __global__ __launch_bounds__(kSipThreads) void sip_kernel(Source source, const float* __restrict__ offsets,
                                                           int32_t* __restrict__ sampled,
                                                           float* __restrict__ weights, int population,
                                                           int samples) {
-    using Reduce = cub::BlockReduce<SumMax, kSipThreads>;
-    using CountScan = cub::BlockScan<int, kSipThreads>;
-    using MassScan = cub::BlockScan<double, kSipThreads>;
-    union Scratch {
-        typename Reduce::TempStorage reduce;
-        typename CountScan::TempStorage count;
-        typename MassScan::TempStorage mass;
-    };
-    __shared__ Scratch scratch;
+    extern __shared__ double prefix[];
+    Scratch& scratch = *reinterpret_cast<Scratch*>(prefix);
     __shared__ double scale;
     __shared__ int certain;
     __shared__ int added;
     __shared__ int last_residual;
     __shared__ int marking;
-    extern __shared__ double prefix[];
 
     const int buckets = (population + kSipBucket - 1) / kSipBucket;
-    float* values = reinterpret_cast<float*>(prefix + buckets + 1);
+    float* values = reinterpret_cast<float*>(reinterpret_cast<unsigned char*>(prefix) + sip_prefix_region(population));
     const int tid = threadIdx.x;
     const int64_t row = blockIdx.x;
     int32_t* out_ids = sampled + row * samples;
@@ -111,16 +83,20 @@ __global__ __launch_bounds__(kSipThreads) void sip_kernel(Source source, const f
 
     // Iterative certainty: mark every unit whose inclusion probability reaches 1
     // (negated in place) until the residual budget is stable (csrc/sip.cu:62-96).
-    do {
-        double local_sum = 0.;
-        double local_max = 0.;
-        for (int j = tid; j < population; j += kSipThreads) {
-            if (values[j] > 0.f) {
-                const double value = fmax(static_cast<double>(values[j]), 1e-30);
-                local_sum += value;
-                local_max = fmax(local_max, value);
-            }
+    // The reference re-sums the uncertain masses after each marking pass; the
+    // units a marking pass leaves unmarked are exactly the terms of that sum,
+    // visited in the same per-thread order, so the marking pass accumulates the
+    // next partial sums itself and each iteration is one pass instead of two.
+    double local_sum = 0.;
+    double local_max = 0.;
+    for (int j = tid; j < population; j += kSipThreads) {
+        if (values[j] > 0.f) {
+            const double value = fmax(static_cast<double>(values[j]), 1e-30);
+            local_sum += value;
+            local_max = fmax(local_max, value);
         }
+    }
+    do {
         const SumMax total = Reduce(scratch.reduce).Reduce(SumMax{local_sum, local_max}, SumMaxOp{});
         if (tid == 0) {
             scale = (samples - certain) / total.sum;
@@ -130,10 +106,18 @@ __global__ __launch_bounds__(kSipThreads) void sip_kernel(Source source, const f
         __syncthreads();
         if (marking) {
             int count = 0;
+            local_sum = 0.;
+            local_max = 0.;
             for (int j = tid; j < population; j += kSipThreads) {
-                if (values[j] > 0.f && fmax(static_cast<double>(values[j]), 1e-30) * scale >= 1.) {
-                    values[j] = -values[j];
-                    ++count;
+                if (values[j] > 0.f) {
+                    const double value = fmax(static_cast<double>(values[j]), 1e-30);
+                    if (value * scale >= 1.) {
+                        values[j] = -values[j];
+                        ++count;
+                    } else {
+                        local_sum += value;
+                        local_max = fmax(local_max, value);
+                    }
                 }
             }
             atomicAdd(&added, count);
@@ -176,6 +160,7 @@ __global__ __launch_bounds__(kSipThreads) void sip_kernel(Source source, const f
         chunk_mass += values[j] > 0.f ? static_cast<double>(values[j]) * scale : 0.;
     double cumulative = 0.;
     MassScan(scratch.mass).ExclusiveSum(chunk_mass, cumulative);
+    __syncthreads();  // the scan's temporaries overlap the prefix written below
     const int residuals = samples - certain;
     if (tid == 0) prefix[buckets] = residuals;
     for (int j = begin; j < end; ++j) {
@@ -217,8 +202,7 @@ __global__ __launch_bounds__(kSipThreads) void sip_kernel(Source source, const f
 }  // namespace
 
 size_t sip_smem_bytes(int64_t population) {
-    const size_t buckets = static_cast<size_t>((population + kSipBucket - 1) / kSipBucket);
-    return population * sizeof(float) + (buckets + 1) * sizeof(double);
+    return sip_prefix_region(population) + static_cast<size_t>(population) * sizeof(float);
 }
 
 int sip_smem_limit() {
@@ -226,11 +210,8 @@ int sip_smem_limit() {
     cudaGetDevice(&device);
     cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, device);
     cudaFuncAttributes attr{};
-    cudaFuncGetAttributes(&attr, sip_kernel<MixedScores>);
-    cudaFuncAttributes attr2{};
-    cudaFuncGetAttributes(&attr2, sip_kernel<DenseScores>);
-    const size_t static_bytes = attr.sharedSizeBytes > attr2.sharedSizeBytes ? attr.sharedSizeBytes : attr2.sharedSizeBytes;
-    return optin - static_cast<int>(static_bytes);
+    cudaFuncGetAttributes(&attr, sip_kernel<DenseScores>);
+    return optin - static_cast<int>(attr.sharedSizeBytes);
 }
 
 template <class Source>
@@ -249,19 +230,6 @@ static cudaError_t launch_sip_impl(const Source& source, const float* offsets, i
 cudaError_t launch_sip(const float* scores, const float* offsets, int64_t rows, int64_t population,
                        int32_t* ids, float* log_weights, int64_t samples, cudaStream_t stream) {
     DenseScores source{scores, population};
-    return launch_sip_impl(source, offsets, rows, population, ids, log_weights, samples, stream);
-}
-
-cudaError_t launch_mix_sip(const half* lse, int64_t ld, const float* populations,
-                           const float* lse_max, const float* lse_den, const float* offsets,
-                           int64_t rows, int64_t population, int32_t* ids, float* log_weights,
-                           int64_t samples, cudaStream_t stream) {
-    MixedScores source{};
-    source.lse = lse;
-    source.ld = ld;
-    source.populations = populations;
-    source.lse_max = lse_max;
-    source.lse_den = lse_den;
     return launch_sip_impl(source, offsets, rows, population, ids, log_weights, samples, stream);
 }
 

@@ -44,8 +44,8 @@ def test_workspace_size_layout():
     assert lib.abx_ibcs_workspace_size(bh, seq, ctypes.byref(out)) == 0
     rows, fine = bh * 591, seq // 4
     ld = (fine + 7) // 8 * 8
-    lse_bytes = rows * 8 * ld * 2
-    assert lse_bytes < out.value < lse_bytes + 2 * 1024 ** 3
+    scratch = rows * 8 * ld * 2 + rows * fine * 4  # fp16 centroid LSEs + f32 block scores
+    assert scratch < out.value < scratch + 2 * 1024 ** 3
 
 
 def test_compute_entry_points_validate_before_launch():
