@@ -100,6 +100,18 @@ class ClockSampler:
                 "reasons": sorted(reasons), "samples": len(sm)}
 
 
+# DRAM bytes (read + write) of one prefill launch per head at the Wan shape, from
+# one ncu capture of the 2-head case (dram__bytes_read.sum + dram__bytes_write.sum
+# = 135.89 + 25.59 MB); a head's K/V stay L2-resident, so traffic scales with heads.
+PREFILL_DRAM_BYTES_PER_HEAD = (135.89e6 + 25.59e6) / 2
+
+
+def plan_bytes(bh: int, tokens: int, samples: int) -> float:
+    """Algorithmic HBM bytes of build_plan: read Q and K once, write ids + weights."""
+    rows = bh * math.ceil(tokens / 128)
+    return 2.0 * bh * tokens * 128 * 2 + rows * samples * 8
+
+
 def layer_flops(bh: int, tokens: int, keys_per_row: int) -> float:
     """4*D*BH*S*keys: QK^T and PV of the sparse prefill (D = 128)."""
     return 4.0 * 128 * bh * tokens * keys_per_row
@@ -111,59 +123,78 @@ def dense_flops(bh: int, tokens: int) -> float:
 
 # ---- CPU baseline (the oracle port, bounded sample) -----------------------------
 
-def cpu_sample(shape, rows_sample: int = 8, threads: int = 1) -> dict:
-    """Time the CPU restatement of the layer on `rows_sample` query blocks of one
-    head (IBCS + SIP + prefill) plus the per-head key pooling, and extrapolate
-    linearly to the whole layer. Returns ms per layer."""
+def _cpu_rows(task) -> tuple[float, float]:
+    """Worker: the CPU restatement of the layer (IBCS + SIP + prefill) on
+    `count` query blocks of one head; returns (pool seconds, rows seconds)."""
+    name, frames, height, width, seed, samples, first, count = task
     import numpy as np
     from threadpoolctl import threadpool_limits
 
+    sys.path.insert(0, str(ROOT))
     from ab_attention_b200.synthetic import smooth_field
     from oracle import oracle
 
-    q, k, v = smooth_field(1, shape.frames, shape.height, shape.width, seed=shape.seed, device="cpu")
-    to_bits = lambda t: t.contiguous().view(torch.int16).numpy().view(np.uint16)  # noqa: E731
-    qbits, kbits = to_bits(q[0:1]), to_bits(k[0:1])
-    tokens = shape.tokens
-    qb = math.ceil(tokens / 128)
-    fine = tokens // 4
-    samples = shape.sample_pages * 32
-    rows_total = shape.batch_heads * qb
-    with threadpool_limits(threads):
+    with threadpool_limits(1):
+        q, k, v = smooth_field(1, frames, height, width, seed=seed, device="cpu")
+        bits = lambda t: t.contiguous().view(torch.int16).numpy().view(np.uint16)  # noqa: E731
+        # per-head work: key pooling and the float64 copies of K and V
         t0 = time.perf_counter()
-        pooled = oracle.pool(kbits)
+        pooled = oracle.pool(bits(k))
+        k64, v64 = k.double().numpy(), v.double().numpy()
         t_pool = time.perf_counter() - t0
-        sub = qbits[:, : rows_sample * 128]
+        sub = bits(q)[:, first * 128:(first + count) * 128]
+        q64 = q[:, first * 128:(first + count) * 128].double().numpy()
+        # per-row work: clustering, centroid scores, mixture, SIP, sparse prefill
         t0 = time.perf_counter()
         cent, pops, _ = oracle.cluster(sub)
-        lse, mx, den = oracle.lse(cent, pooled, 1, rows_sample)
+        lse, mx, den = oracle.lse(cent, pooled, 1, count)
         scores = oracle.mix(lse, pops, mx, den)
-        ids, logw = oracle.sip(scores, np.full(rows_sample, 0.5, np.float32), samples)
-        t_plan = time.perf_counter() - t0
-        t0 = time.perf_counter()
-        qf = q[0:1, : rows_sample * 128].float().numpy()
-        oracle.prefill(qf, k[0:1].float().numpy(), v[0:1].float().numpy(), ids, logw)
-        t_prefill = time.perf_counter() - t0
-    per_row = (t_plan + t_prefill) / rows_sample
-    ms = (per_row * rows_total + t_pool * shape.batch_heads) * 1e3
-    return {"value": ms, "unit": "ms", "cores": threads,
-            "sample": f"{rows_sample} query blocks of 1 head (IBCS+SIP+prefill) + key pooling of 1 head, "
+        ids, logw = oracle.sip(scores, np.full(count, 0.5, np.float32), samples)
+        oracle.prefill(q64, k64, v64, ids, logw)
+        t_rows = time.perf_counter() - t0
+    return t_pool, t_rows
+
+
+def cpu_sample(shape, rows_per_worker: int = 24, workers: int = 1) -> dict:
+    """Time the CPU restatement on a bounded sample (rows_per_worker query blocks
+    per worker process, plus one head's key pooling per worker) and extrapolate
+    linearly to the whole layer. Returns ms per layer."""
+    qb = math.ceil(shape.tokens / 128)
+    rows_total = shape.batch_heads * qb
+    tasks = [(shape.name, shape.frames, shape.height, shape.width, shape.seed, shape.sample_pages * 32,
+              (w * rows_per_worker) % max(1, qb - rows_per_worker), rows_per_worker) for w in range(workers)]
+    t0 = time.perf_counter()
+    if workers == 1:
+        results = [_cpu_rows(tasks[0])]
+    else:
+        import concurrent.futures as cf
+        import multiprocessing as mp
+
+        with cf.ProcessPoolExecutor(max_workers=workers, mp_context=mp.get_context("spawn")) as pool:
+            results = list(pool.map(_cpu_rows, tasks))
+    wall = time.perf_counter() - t0
+    t_pool = statistics.mean(r[0] for r in results)
+    t_rows = statistics.mean(r[1] for r in results)
+    # each worker handles its own rows in parallel: rows/s = workers * rows_per_worker / t_rows
+    ms = (rows_total * t_rows / (workers * rows_per_worker) + shape.batch_heads * t_pool / workers) * 1e3
+    return {"value": ms, "unit": "ms", "cores": workers,
+            "sample": f"{rows_per_worker} query blocks of one head per worker x {workers} worker(s) "
+                      f"(C oracle: IBCS + SIP; float64 numpy prefill) + that head's key pooling, "
                       f"extrapolated linearly to {rows_total} blocks / {shape.batch_heads} heads",
-            "sample_seconds": t_pool + t_plan + t_prefill}
+            "sample_seconds": wall}
 
 
 def run_reference(args, shape) -> None:
-    """`--impl reference`: the reference math on the host cores (the oracle port;
-    the reference's only CPU path is its PyTorch-free math, which it runs on the GPU)."""
+    """`--impl reference`: the reference's math on the host cores. The reference
+    has no CPU implementation of its own (its kernels are CUDA), so this arm
+    runs the CPU restatement in oracle/ with one worker process per core."""
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
     cores = os.cpu_count() or 1
-    values = []
     for _ in range(args.warmup):
-        cpu_sample(shape, rows_sample=2, threads=cores)
-    for _ in range(args.steps):
-        values.append(cpu_sample(shape, rows_sample=4, threads=cores)["value"])
+        cpu_sample(shape, rows_per_worker=1, workers=cores)
+    values = [cpu_sample(shape, rows_per_worker=4, workers=cores)["value"] for _ in range(args.steps)]
     value = statistics.median(values)
     line = {
         "impl": "reference", "metric": METRIC, "value": value, "unit": "ms", "n_gpus": args.gpus,
@@ -172,7 +203,8 @@ def run_reference(args, shape) -> None:
         "config": {"workload": shape.name, "batch": shape.batch, "heads": shape.heads, "tokens": shape.tokens,
                    "sample_pages": shape.sample_pages},
         "cpu_baseline": {"value": value, "unit": "ms", "cores": cores, "kind": "port",
-                         "sample": "4 query blocks of 1 head per step (C/numpy restatement), extrapolated"},
+                         "sample": f"4 query blocks of one head per worker x {cores} workers per step "
+                                   f"(C/numpy restatement of the reference math), extrapolated to the layer"},
         "e2e": {"value": value, "unit": "ms", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
@@ -215,22 +247,17 @@ def main() -> None:
     device = torch.device("cuda", local)
     if world > 1:
         dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=device)
+    from ab_attention_b200 import shard
+
     bh = shape.batch_heads
-    if bh % world:
-        raise SystemExit(f"{bh} heads do not split over {world} GPUs")
-    per = bh // world
-    shard = slice(rank * per, (rank + 1) * per)
-    q, k, v, text = make_inputs(shape, device=device, bh_slice=shard if world > 1 else None)
+    heads = shard.head_slice(bh, world, rank)
+    per = heads.stop - heads.start
+    q, k, v, text = make_inputs(shape, device=device, bh_slice=heads if world > 1 else None)
     q, k, v = (x.reshape(1, per, shape.tokens, 128).contiguous() for x in (q, k, v))
     if text is not None:
         text = tuple(t.reshape(1, per, -1, 128).contiguous() for t in text)
     tokens = shape.tokens
-    qb = math.ceil(tokens / 128)
-    rows_global = bh * qb
-    gen = torch.Generator(device=device).manual_seed(shape.seed)
-    offsets_all = torch.rand(rows_global, device=device, generator=gen)
-    offsets = offsets_all[rank * per * qb:(rank + 1) * per * qb].contiguous()
-    out_full = torch.empty((world * per, tokens, 128), dtype=torch.bfloat16, device=device) if world > 1 else None
+    offsets = shard.shard_offsets(shard.layer_offsets(bh, tokens, shape.seed, device), tokens, heads)
 
     def barrier():
         if world > 1:
@@ -250,7 +277,7 @@ def main() -> None:
         if e:
             e[2].record(stream)
         if world > 1:
-            dist.all_gather_into_tensor(out_full, o.reshape(per, tokens, 128))
+            shard.gather_heads(o.reshape(per, tokens, 128), world)
         if e:
             e[3].record(stream)
         return o
@@ -356,8 +383,16 @@ def main() -> None:
         "plan_amortised_ms": prefill_ms + plan_ms / 4 + gather_ms,
         "roofline": {"kernel": "sparse prefill", "bound": "tensor", "achieved": achieved,
                      "peak": peaks["bf16_tflops_sustained"], "unit": "TFLOP/s",
-                     "frac": achieved / peaks["bf16_tflops_sustained"], "traffic": None,
+                     "frac": achieved / peaks["bf16_tflops_sustained"],
+                     "traffic": (PREFILL_DRAM_BYTES_PER_HEAD * per if shape.name.startswith("wan14b") else None),
                      "peak_source": peaks["source"] + " sustained bf16"},
+        "plan_roofline": {"kernels": "cluster+pool+lse+mix+sip", "bound": "hbm",
+                          "achieved": plan_bytes(per, tokens, shape.sample_pages * 32) / (plan_ms * 1e-3) / 1e9,
+                          "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                          "frac": plan_bytes(per, tokens, shape.sample_pages * 32) / (plan_ms * 1e-3) / 1e9
+                          / peaks["hbm_gbs"],
+                          "note": "algorithmic bytes (Q, K in; plan out); the kernels are bound by the exact "
+                                  "fast-math exp2/log2/division work and the double-precision SIP sums"},
         "gpu_launches": 5 * args.steps,
         "clocks": clocks.summary(),
         **dense,
@@ -365,7 +400,7 @@ def main() -> None:
     if e2e is not None:
         line["e2e"] = e2e
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        line["cpu_baseline"] = cpu_sample(shape)
+        line["cpu_baseline"] = cpu_sample(shape, rows_per_worker=96, workers=1)
         line["cpu_baseline"]["kind"] = "port"
     if rank == 0:
         print(json.dumps(line), flush=True)

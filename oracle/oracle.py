@@ -148,9 +148,9 @@ def prefill(q, k, v, ids, log_weights, text_k=None, text_v=None):
     lse = np.zeros((bh, seq))
     offs = np.arange(4)
     for h in range(bh):
-        qh = q[h].astype(np.float64)
-        kh = k[h].astype(np.float64)
-        vh = v[h].astype(np.float64)
+        qh = np.asarray(q[h], dtype=np.float64)
+        kh = np.asarray(k[h], dtype=np.float64)
+        vh = np.asarray(v[h], dtype=np.float64)
         for r in range(qb):
             row = h * qb + r
             tok = (4 * ids[row][:, None] + offs[None, :]).reshape(-1)

@@ -1,0 +1,104 @@
+"""Head-sharded execution across ranks, on CPU with the gloo backend.
+
+The per-head computation is replaced by a deterministic CPU stand-in (the
+kernels need a GPU); what is tested is the sharding contract: contiguous head
+slices, offsets drawn for the whole layer then sliced (so plans do not depend
+on the number of ranks), and one all-gather in rank order. A rank that fails
+before the collective makes the others error out within the process-group
+timeout instead of hanging.
+"""
+import math
+import os
+import socket
+from datetime import timedelta
+
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+from ab_attention_b200 import shard
+
+BH, TOKENS, SEED = 8, 600, 5
+
+
+def _per_head(x: torch.Tensor, offsets: torch.Tensor) -> torch.Tensor:
+    """Stand-in for one head's layer: depends on the head's input and its rows' offsets."""
+    qb = math.ceil(x.shape[0] / 128)
+    scale = offsets.reshape(qb).repeat_interleave(128)[: x.shape[0]]
+    return x * scale[:, None] + x.sum()
+
+
+def _reference():
+    gen = torch.Generator().manual_seed(0)
+    x = torch.randn(BH, TOKENS, 4, generator=gen)
+    offsets = shard.layer_offsets(BH, TOKENS, SEED, "cpu")
+    qb = math.ceil(TOKENS / 128)
+    out = torch.stack([_per_head(x[h], offsets[h * qb:(h + 1) * qb]) for h in range(BH)])
+    return x, out
+
+
+def _free_port() -> int:
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _worker(rank, world, port, result_path, fail_rank):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=timedelta(seconds=10))
+    try:
+        x, _ = _reference()
+        heads = shard.head_slice(BH, world, rank)
+        offsets = shard.shard_offsets(shard.layer_offsets(BH, TOKENS, SEED, "cpu"), TOKENS, heads)
+        qb = math.ceil(TOKENS / 128)
+        if rank == fail_rank:
+            raise RuntimeError("injected failure before the all-gather")
+        local = torch.stack([_per_head(x[h], offsets[i * qb:(i + 1) * qb])
+                             for i, h in enumerate(range(heads.start, heads.stop))])
+        try:
+            full = shard.gather_heads(local, world)
+            status = "ok"
+        except Exception as exc:  # noqa: BLE001
+            full, status = None, f"error: {type(exc).__name__}"
+        if rank == 0:
+            torch.save({"status": status, "full": full}, result_path)
+    finally:
+        try:
+            dist.destroy_process_group()
+        except Exception:  # noqa: BLE001
+            pass
+
+
+@pytest.mark.parametrize("world", [2, 4])
+def test_sharded_layer_matches_single_process(tmp_path, world):
+    path = str(tmp_path / "out.pt")
+    mp.start_processes(_worker, args=(world, _free_port(), path, -1), nprocs=world, join=True,
+                       start_method="spawn")
+    result = torch.load(path)
+    _, want = _reference()
+    assert result["status"] == "ok"
+    assert torch.equal(result["full"], want)
+
+
+def test_plan_offsets_do_not_depend_on_world_size():
+    full = shard.layer_offsets(BH, TOKENS, SEED, "cpu")
+    qb = math.ceil(TOKENS / 128)
+    for world in (1, 2, 4, 8):
+        parts = [shard.shard_offsets(full, TOKENS, shard.head_slice(BH, world, r)) for r in range(world)]
+        assert torch.equal(torch.cat(parts), full)
+        assert all(p.numel() == BH // world * qb for p in parts)
+    with pytest.raises(ValueError):
+        shard.head_slice(BH, 3, 0)
+
+
+def test_failed_rank_surfaces_as_error_not_hang(tmp_path):
+    path = str(tmp_path / "out.pt")
+    ctx = mp.start_processes(_worker, args=(2, _free_port(), path, 1), nprocs=2, join=False,
+                             start_method="spawn")
+    with pytest.raises(Exception):
+        while not ctx.join(timeout=60):
+            pass
+    # rank 0 either recorded an error from the collective or never wrote a result
+    if os.path.exists(path):
+        assert torch.load(path)["status"].startswith("error")
