@@ -95,15 +95,16 @@ def _check_qkv(q, k, v):
 
 
 @torch.no_grad()
-def apply_plan(q, k, v, plan, *, return_lse=False, text_kv=None):
-    """HT-weighted sparse attention of Q over the plan's sampled KV4 blocks.
+def paged_attention(q, k, v, descriptor, log_weights, *, return_lse=False, text_kv=None):
+    """Weighted sparse attention over a plan's KV4 ids (flashinfer_backend.py:164-242).
 
-    ``text_kv=(text_k, text_v)`` ([B,H,T,128] bf16, T % 4 == 0) appends T keys
-    that every query block always includes with weight pi = 1. The optional
-    base-2 LSE is returned as a [batch, heads, tokens] float32 tensor.
+    Same signature, checks and outputs as the reference's FlashInfer adapter;
+    the work is one tcgen05 kernel launch. ``text_kv=(text_k, text_v)``
+    ([B,H,T,128] bf16, T % 4 == 0) appends T keys that every query block always
+    includes with weight pi = 1. The optional base-2 LSE is [batch, heads, tokens]
+    float32.
     """
     _check_qkv(q, k, v)
-    descriptor, log_weights = plan
     batch, heads, tokens, dim = q.shape
     batch_heads = batch * heads
     rows = batch_heads * math.ceil(tokens / 128)
@@ -132,6 +133,17 @@ def apply_plan(q, k, v, plan, *, return_lse=False, text_kv=None):
     if not return_lse:
         return out
     return out, lse.reshape(batch, heads, tokens)
+
+
+@torch.no_grad()
+def apply_plan(q, k, v, plan, *, return_lse=False, text_kv=None):
+    """HT-weighted sparse attention of Q over the plan's sampled KV4 blocks
+    (attention.py:85-96): ``paged_attention(q, k, v, *plan)``.
+
+    A plan can be reused across denoising steps while the shape and device stay
+    the same. See ``paged_attention`` for ``text_kv`` and the LSE.
+    """
+    return paged_attention(q, k, v, *plan, return_lse=return_lse, text_kv=text_kv)
 
 
 @torch.no_grad()

@@ -184,3 +184,25 @@ def dense_prefill(q3, k3, v3, *, return_lse=False):
         _lib.check(lib.abx_dense_prefill(_lib.ptr(q3), _lib.ptr(k3), _lib.ptr(v3), bh, seq, _lib.ptr(o),
                                          _lib.ptr(lse_), _lib.stream_of(q3)), "abx_dense_prefill")
     return o, lse_
+
+
+# ---- torch.library registration ------------------------------------------------------
+# `torch.ops.ab_attention.{ibcs,sip,sparse_prefill}`: the custom-op form of the
+# same entry points, with a CUDA kernel only. A CPU tensor finds no kernel and
+# raises, so there is no silent fallback.
+
+@torch.library.custom_op("ab_attention::ibcs", mutates_args=(), device_types="cuda")
+def _ibcs_op(q: torch.Tensor, k: torch.Tensor) -> torch.Tensor:
+    return ibcs(q, k)
+
+
+@torch.library.custom_op("ab_attention::sip", mutates_args=("ids", "logs"), device_types="cuda")
+def _sip_op(scores: torch.Tensor, offsets: torch.Tensor, ids: torch.Tensor, logs: torch.Tensor) -> None:
+    sip(scores, offsets, ids, logs)
+
+
+@torch.library.custom_op("ab_attention::sparse_prefill", mutates_args=(), device_types="cuda")
+def _sparse_prefill_op(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, ids: torch.Tensor,
+                       log_weights: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
+    """[BH,S,128] bf16 q/k/v, ids/log_weights [rows, samples] -> (o, base-2 lse [BH,S])."""
+    return sparse_prefill(q, k, v, ids, log_weights, return_lse=True)

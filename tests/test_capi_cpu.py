@@ -63,3 +63,30 @@ def test_compute_entry_points_validate_before_launch():
     # prefill: negative text tokens, samples beyond F
     assert lib.abx_sparse_prefill(p, p, p, 1, 1024, p, p, 300, None, None, 0, p, None, None) == 1
     assert lib.abx_sparse_prefill(p, p, p, 1, 1024, p, p, 8, None, None, -4, p, None, None) == 1
+
+
+def test_torch_ops_registered_without_cpu_kernel():
+    import torch
+
+    import ab_attention_b200  # noqa: F401  (registers torch.ops.ab_attention)
+
+    q = torch.zeros(1, 1, 256, 128, dtype=torch.bfloat16)
+    for call in (lambda: torch.ops.ab_attention.ibcs(q, q),
+                 lambda: torch.ops.ab_attention.sparse_prefill(q[0], q[0], q[0],
+                                                               torch.zeros(2, 32, dtype=torch.int32),
+                                                               torch.zeros(2, 32))):
+        with pytest.raises(NotImplementedError):
+            call()
+
+
+def test_python_api_refuses_cpu_tensors():
+    import torch
+
+    from ab_attention_b200 import apply_plan, build_plan
+
+    q = torch.zeros(1, 1, 1024, 128, dtype=torch.bfloat16)
+    with pytest.raises(RuntimeError):
+        build_plan(q, q, sample_pages=2)
+    plan = (torch.zeros(8, 2, 32, dtype=torch.int32), torch.zeros(8, 2, 32))
+    with pytest.raises(ValueError):
+        apply_plan(q, q, q, plan)

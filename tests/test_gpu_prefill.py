@@ -113,3 +113,29 @@ def test_sparse_prefill_matches_torch_fp32_reference():
             out[h, r * 128:(r + 1) * 128] = p @ vals
     err = (o[0].float() - out).abs()
     assert err.max().item() <= MAX_ERR and err.mean().item() <= MEAN_ERR
+
+
+def test_torch_ops_and_paged_attention_match_python_api():
+    from ab_attention_b200 import ops
+    from ab_attention_b200.attention import paged_attention
+
+    bh, grid = 2, (2, 16, 32)
+    q, k, v = smooth_field(bh, *grid, seed=11, device="cuda")
+    q4, k4, v4 = (x.unsqueeze(0) for x in (q, k, v))
+    plan = build_plan(q4, k4, sample_pages=2, seed=9)
+    o, lse = apply_plan(q4, k4, v4, plan, return_lse=True)
+    o2, lse2 = paged_attention(q4, k4, v4, plan.descriptor, plan.log_weights, return_lse=True)
+    assert torch.equal(o, o2) and torch.equal(lse, lse2)
+    rows = plan.descriptor.shape[0]
+    ids = plan.descriptor.reshape(rows, -1).contiguous()
+    logw = plan.log_weights.reshape(rows, -1).contiguous()
+    o3, lse3 = torch.ops.ab_attention.sparse_prefill(q, k, v, ids, logw)
+    assert torch.equal(o3, o[0]) and torch.equal(lse3, lse[0])
+    scores = torch.ops.ab_attention.ibcs(q4, k4)
+    assert torch.equal(scores, ops.ibcs(q4, k4))
+    gen = torch.Generator(device="cuda").manual_seed(9)
+    offsets = torch.rand(rows, device="cuda", generator=gen)
+    ids2 = torch.empty_like(ids)
+    logw2 = torch.empty_like(logw)
+    torch.ops.ab_attention.sip(scores, offsets, ids2, logw2)
+    assert torch.equal(ids2, ids) and torch.equal(logw2, logw)
