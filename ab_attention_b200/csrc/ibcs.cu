@@ -5,17 +5,20 @@
 // are kept identical so the downstream page selection is bit-exact):
 //   cluster_kernel  <- cluster_queries_kernel  csrc/ibcs.cu:106-238
 //   pool_kernel     <- pool_keys_kernel        csrc/ibcs.cu:244-266
-//   lse_kernel      <- ibcs_lse_kernel         csrc/ibcs.cu:370-489
+//   lse_kernel      <- ibcs_lse_kernel         csrc/ibcs.cu:370-489 (tcgen05 + TMEM)
 //   mix_kernel      <- ibcs_scores_kernel      csrc/ibcs.cu:495-538
 //
 // What differs is the work decomposition: one thread per query for the
 // clustering distances (the 32-lane partial sums and the xor-butterfly are
 // evaluated inside the thread, in the reference's order), 16-byte vector
-// loads and stores throughout, 128 centroid rows per CTA in the scorer with a
-// 64-block key tile, and a padded fp16 LSE scratch written in 128-byte rows.
+// loads and stores throughout, the scorer on tcgen05 (TMA key tiles, TMEM
+// accumulators, one thread per centroid row running the reference's four
+// lane-class chains), and a padded fp16 LSE scratch with 16-byte aligned rows.
 // This file must be compiled with --use_fast_math (as csrc/ibcs.cu is).
 #include "common.cuh"
 #include "ibcs.cuh"
+#include "tcgen05.cuh"
+#include "tma_host.cuh"
 
 #include <cfloat>
 #include <cmath>
@@ -228,27 +231,100 @@ __global__ __launch_bounds__(256) void pool_kernel(const bf16* __restrict__ k, i
 }
 
 // ---------------------------------------------------------------------------
-// Centroid x pooled-key scoring with per-centroid normalizers.
+// Centroid x pooled-key scoring with per-centroid normalizers (tcgen05).
+//
+// One CTA scores 128 scaled-centroid rows of one head against every pooled key
+// of that head: S = C K^T on the tensor cores (M = 128 rows, N = 64 keys = 32
+// KV4 blocks per tile, K = 128 in eight k16 steps, f32 accumulators in TMEM),
+// with the reference's epilogue per element. tcgen05.mma with this shape
+// accumulates bit-identically to the reference's chain of eight
+// mma.sync.m16n8k16 (checked on this hardware over 2M products, and covered
+// by the bit-exact tests against the reference kernels).
+//
+//   warps 0-3  epilogue: thread m owns centroid row m (TMEM lane m) and reads
+//              its row's 64 accumulators per tile; per KV4 block it forms the
+//              pair LSE, rounds it to fp16, stores it, and folds it into one of
+//              four running (max, den) chains by block index mod 4 (the
+//              reference's four lane classes, csrc/ibcs.cu:329-335,454-462),
+//              merged at the end as (c0 + c1) + (c2 + c3) (:468-477).
+//   warp 4     TMA: the 32 KB centroid tile once, then 16 KB key tiles into a
+//              3-stage ring; allocates and frees TMEM.
+//   warp 5     one thread issues the MMAs into two TMEM buffers.
 // ---------------------------------------------------------------------------
 
-constexpr int kLseWarps = 8;
-constexpr int kLseThreads = kLseWarps * 32;
-constexpr int kLseRowsPerCta = 16 * kLseWarps;  // centroid rows per CTA
-constexpr int kLseTileBlocks = 64;              // KV4 blocks per key tile
-constexpr int kLseTileKeys = kLseTileBlocks * kReps;
-constexpr int kLseStageChunks = kLseTileKeys * 16;  // 16-byte chunks per stage (32 KB)
-constexpr int kLseStagingStride = kLseTileBlocks + 8;  // padded row (144 B) avoids bank conflicts
-constexpr int kLseStagingHalfs = 16 * kLseStagingStride;  // per-warp LSE staging tile
+constexpr int kLseRows = 128;                          // centroid rows per CTA = TMEM lanes
+constexpr int kLseTileBlocks = 32;                     // KV4 blocks per key tile
+constexpr int kLseTileKeys = kLseTileBlocks * kReps;  // 64 pooled rows = MMA N
+constexpr int kLseStages = 3;
+constexpr int kLseLoadWarp = 4;
+constexpr int kLseMmaWarp = 5;
+constexpr int kLseThreads = 6 * 32;
+constexpr uint32_t kLseSlabA = kLseRows * 128;      // 128 rows x 64 bf16
+constexpr uint32_t kLseSlabB = kLseTileKeys * 128;  // 64 rows x 64 bf16
+constexpr uint32_t kLseStageBytes = 2 * kLseSlabB;
+constexpr uint32_t kLseOffA = 0;
+constexpr uint32_t kLseOffB = 2 * kLseSlabA;
+constexpr uint32_t kLseOffBar = kLseOffB + kLseStages * kLseStageBytes;
+constexpr int kLseBarAFull = 0;
+constexpr int kLseBarBFull = 1;                            // kLseStages
+constexpr int kLseBarBEmpty = kLseBarBFull + kLseStages;  // kLseStages
+constexpr int kLseBarTFull = kLseBarBEmpty + kLseStages;  // 2 TMEM buffers
+constexpr int kLseBarTEmpty = kLseBarTFull + 2;           // 2
+constexpr int kLseBarDrain = kLseBarTEmpty + 2;
+constexpr int kLseNumBars = kLseBarDrain + 1;
+constexpr uint32_t kLseOffTmemSlot = kLseOffBar + kLseNumBars * 8;
+constexpr uint32_t kLseOffAbort = kLseOffTmemSlot + 4;
+constexpr uint32_t kLseSmemBytes = kLseOffAbort + 4 + 1024;  // slack for aligning the base
+constexpr uint32_t kLseTmemColumns = 2 * kLseTileKeys;
+constexpr uint32_t kLseIdesc = tc::idesc_bf16_f32(kLseRows, kLseTileKeys, 0, 0);  // both K-major
+constexpr uint64_t kLseWaitLimit = 400ull * 1000 * 1000;  // SM cycles per wait (~0.2 s)
 
-__device__ __forceinline__ void accumulate_lse(float& maximum, float& denominator, float value) {
-    const float next_max = fmaxf(maximum, value);
-    denominator = denominator * exp2f(maximum - next_max) + exp2f(value - next_max);
-    maximum = next_max;
+struct LseMaps {
+    CUtensorMap centroids;  // [bh * qb * 8, 128], box 64 x 128 rows
+    CUtensorMap keys;       // [bh * F * 2, 128], box 64 x 64 rows
+};
+
+struct LseArgs {
+    int64_t head_rows;  // qb * 8
+    int64_t ld;         // fp16 LSE row stride (elements)
+    int fine_blocks;
+    int tiles;
+    half* lse;
+    float* lse_max;
+    float* lse_den;
+    int* error;
+    bool vector_rows;   // every LSE row starts on a 16-byte boundary
+};
+
+// 2^(x - x) without a MUFU op: x * 0 + 1 is exactly 1 for finite x (and ex2 of
+// +/-0 is exactly 1, a documented special value of ex2.approx); for an infinite
+// or NaN x both are NaN. Inline PTX keeps the compiler from folding x * 0.
+__device__ __forceinline__ float unit_exp(float x) {
+    float r;
+    asm("fma.rn.f32 %0, %1, 0f00000000, 0f3F800000;" : "=f"(r) : "f"(x));
+    return r;
 }
 
+// The reference's pair_lse (csrc/ibcs.cu:339-343):
+//   M = fmax(l, r); M + log2(fmax(2^(l - M) + 2^(r - M), 1e-20)).
+// The term of the operand equal to M is 2^(M - M) = unit_exp(M); the other is
+// 2^(-|l - r|) (l - r and r - l differ only in sign); the addition commutes.
 __device__ __forceinline__ float pair_lse(float left, float right) {
     const float maximum = fmaxf(left, right);
-    return maximum + log2f(fmaxf(exp2f(left - maximum) + exp2f(right - maximum), 1.0e-20f));
+    return maximum + log2f(fmaxf(unit_exp(maximum) + exp2f(-fabsf(left - right)), 1.0e-20f));
+}
+
+// The reference's accumulate_lse (csrc/ibcs.cu:329-335):
+//   next = fmax(max, v); den = den * 2^(max - next) + 2^(v - next); max = next.
+// One exponent is next - next (ex2 = unit_exp(next)), the other -|max - v|;
+// the multiply-add keeps the reference's shape (one FFMA).
+__device__ __forceinline__ void accumulate_lse(float& maximum, float& denominator, float value) {
+    const float next_max = fmaxf(maximum, value);
+    const bool keep = next_max == maximum;
+    const float e = exp2f(-fabsf(maximum - value));
+    const float unit = unit_exp(next_max);
+    denominator = denominator * (keep ? unit : e) + (keep ? e : unit);
+    maximum = next_max;
 }
 
 __device__ __forceinline__ void combine_lse(float& maximum, float& denominator, float other_max,
@@ -258,149 +334,209 @@ __device__ __forceinline__ void combine_lse(float& maximum, float& denominator, 
     maximum = next;
 }
 
-__device__ __forceinline__ void stage_key_tile(const bf16* __restrict__ pooled_head, uint4* stage,
-                                               int tile, int fine_blocks) {
-    // 128 pooled rows x 16 chunks; rows past the end are clamped to the last block
-    // (their results are never stored, csrc/ibcs.cu:318,355).
-    const int last_key = fine_blocks * kReps - 1;
+// One tile of a row: 32 KV4 blocks from 64 accumulators (block k = columns 2k,
+// 2k + 1: the two pooled representatives). kFull: all 32 blocks are < F.
+template <bool kFull>
+__device__ __forceinline__ void lse_tile(const uint32_t (&acc)[32], int j0, int fine_blocks, half* out,
+                                         bool store, bool vector_rows, float (&mx)[4], float (&dn)[4]) {
 #pragma unroll
-    for (int it = 0; it < kLseStageChunks / kLseThreads; ++it) {
-        const int idx = it * kLseThreads + threadIdx.x;
-        const int key = idx >> 4;
-        const int c = idx & 15;
-        int src_key = tile * kLseTileKeys + key;
-        if (src_key > last_key) src_key = (last_key & ~1) + (key & 1);
-        cp_async_16(stage + chunk_slot(key, c), pooled_head + static_cast<int64_t>(src_key) * kHeadDim + c * 8);
+    for (int q = 0; q < 2; ++q) {
+        uint32_t packed[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+            const int k = 8 * q + 2 * e;
+            const float p0 = pair_lse(__uint_as_float(acc[2 * k]) + 1.0f, __uint_as_float(acc[2 * k + 1]) + 1.0f);
+            const float p1 =
+                pair_lse(__uint_as_float(acc[2 * k + 2]) + 1.0f, __uint_as_float(acc[2 * k + 3]) + 1.0f);
+            // One packed cvt.rn.f16x2 rounds both (the same round-to-nearest as a
+            // scalar conversion); the rounded values are what the chains see.
+            const half2 h = __floats2half2_rn(p0, p1);
+            const float2 r = __half22float2(h);
+            const int j = j0 + k;       // j % 4 == 2 * (e & 1)
+            const int c = 2 * (e & 1);
+            if (kFull || j < fine_blocks) accumulate_lse(mx[c], dn[c], r.x);
+            if (kFull || j + 1 < fine_blocks) accumulate_lse(mx[c + 1], dn[c + 1], r.y);
+            packed[e] = *reinterpret_cast<const uint32_t*>(&h);
+        }
+        const int jb = j0 + 8 * q;
+        if (store && (kFull || jb < fine_blocks)) {
+            if (vector_rows) {
+                // jb < F and jb % 8 == 0, so [jb, jb + 8) lies inside the row's ld = round_up(F, 8).
+                *reinterpret_cast<uint4*>(out + jb) = make_uint4(packed[0], packed[1], packed[2], packed[3]);
+            } else {
+                const half* hv = reinterpret_cast<const half*>(packed);
+#pragma unroll
+                for (int i = 0; i < 8; ++i)
+                    if (kFull || jb + i < fine_blocks) out[jb + i] = hv[i];
+            }
+        }
     }
 }
 
-__global__ __launch_bounds__(kLseThreads) void lse_kernel(
-    const bf16* __restrict__ scaled, const bf16* __restrict__ pooled, int64_t qb, int fine_blocks,
-    int64_t ld, half* __restrict__ lse, float* __restrict__ lse_max, float* __restrict__ lse_den) {
-    extern __shared__ __align__(128) uint4 smem[];
-    uint4* stage0 = smem;
-    uint4* stage1 = smem + kLseStageChunks;
+// grid (ceil(qb * 8 / 128), bh)
+__global__ __launch_bounds__(kLseThreads, 2) void lse_kernel(const __grid_constant__ LseMaps maps,
+                                                             const LseArgs args) {
+    extern __shared__ __align__(1024) unsigned char lse_smem[];
+    const uint32_t raw = smem_addr(lse_smem);
+    const uint32_t base = (raw + 1023u) & ~1023u;
+    unsigned char* base_ptr = lse_smem + (base - raw);
+    auto bar = [&](int i) { return base + kLseOffBar + 8u * static_cast<uint32_t>(i); };
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(base_ptr + kLseOffAbort);
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(base_ptr + kLseOffTmemSlot);
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
-    half* staging = reinterpret_cast<half*>(smem + 2 * kLseStageChunks) + warp * kLseStagingHalfs;
     const int64_t head = blockIdx.y;
-    const int64_t head_rows = qb * kCentroids;
-    const int64_t m0 = static_cast<int64_t>(blockIdx.x) * kLseRowsPerCta + warp * 16;
-    const int g = lane >> 2;
-    const int t = lane & 3;
-    const bf16* pooled_head = pooled + head * static_cast<int64_t>(fine_blocks) * kReps * kHeadDim;
+    const int64_t row0 = static_cast<int64_t>(blockIdx.x) * kLseRows;
+    const int tiles = args.tiles;
 
-    stage_key_tile(pooled_head, stage0, 0, fine_blocks);
-    cp_async_commit();
-
-    // A fragments: 16 scaled-centroid rows x 128 dims; rows past the head are zero.
-    uint32_t a[8][4];
-    {
-        const bf16* base = scaled + head * head_rows * kHeadDim;
-        const int64_t lo = m0 + g, hi = m0 + g + 8;
-#pragma unroll
-        for (int kk = 0; kk < 8; ++kk) {
-            const int col = 16 * kk + 2 * t;
-            a[kk][0] = lo < head_rows ? *reinterpret_cast<const uint32_t*>(base + lo * kHeadDim + col) : 0u;
-            a[kk][1] = hi < head_rows ? *reinterpret_cast<const uint32_t*>(base + hi * kHeadDim + col) : 0u;
-            a[kk][2] = lo < head_rows ? *reinterpret_cast<const uint32_t*>(base + lo * kHeadDim + col + 8) : 0u;
-            a[kk][3] = hi < head_rows ? *reinterpret_cast<const uint32_t*>(base + hi * kHeadDim + col + 8) : 0u;
+    if (threadIdx.x == 0) {
+        *abort_flag = 0;
+        tc::mbar_init(bar(kLseBarAFull), 1);
+        for (int s = 0; s < kLseStages; ++s) {
+            tc::mbar_init(bar(kLseBarBFull + s), 1);
+            tc::mbar_init(bar(kLseBarBEmpty + s), 1);
         }
+        for (int b = 0; b < 2; ++b) {
+            tc::mbar_init(bar(kLseBarTFull + b), 1);
+            tc::mbar_init(bar(kLseBarTEmpty + b), kLseRows);
+        }
+        tc::mbar_init(bar(kLseBarDrain), 1);
+        tc::mbar_init_fence();
     }
+    if (warp == kLseLoadWarp) {
+        tc::tmem_alloc(smem_addr(tmem_slot), kLseTmemColumns);
+        tc::tmem_relinquish();
+    }
+    tc::fence_before_sync();
+    __syncthreads();
+    tc::fence_after_sync();
+    const uint32_t tmem = *tmem_slot;
 
-    // Running normalizers for rows g and g+8, lane class t = KV4 block index mod 4.
-    float maximum[2] = {-FLT_MAX, -FLT_MAX};
-    float denominator[2] = {0.0f, 0.0f};
-    const int tiles = static_cast<int>(ceil_div(fine_blocks, kLseTileBlocks));
-    const bool vec_store = (ld % 8) == 0;
-
-    for (int tile = 0; tile < tiles; ++tile) {
-        uint4* current = (tile & 1) ? stage1 : stage0;
-        uint4* upcoming = (tile & 1) ? stage0 : stage1;
-        cp_async_wait<0>();
-        __syncthreads();
-        if (tile + 1 < tiles) {
-            stage_key_tile(pooled_head, upcoming, tile + 1, fine_blocks);
-            cp_async_commit();
-        }
-        const uint32_t stage_base = smem_addr(current);
-#pragma unroll 2
-        for (int grp = 0; grp < kLseTileKeys / 16; ++grp) {
-            float acc[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
-            const int key = grp * 16 + (lane >> 4) * 8 + (lane & 7);
-#pragma unroll
-            for (int kk = 0; kk < 8; ++kk) {
-                const int c = 2 * kk + ((lane >> 3) & 1);
-                uint32_t b[4];
-                ldmatrix_x4(b, stage_base + chunk_slot(key, c) * 16);
-                mma_bf16_16816(acc[0], a[kk], b[0], b[1]);
-                mma_bf16_16816(acc[1], a[kk], b[2], b[3]);
+    if (warp == kLseLoadWarp) {
+        if (lane == 0) {
+            tc::mbar_arrive_expect_tx(bar(kLseBarAFull), 2 * kLseSlabA);
+            const int32_t ay = static_cast<int32_t>(head * args.head_rows + row0);
+            tc::tma_load_2d(base + kLseOffA, &maps.centroids, 0, ay, bar(kLseBarAFull));
+            tc::tma_load_2d(base + kLseOffA + kLseSlabA, &maps.centroids, 64, ay, bar(kLseBarAFull));
+            const int64_t key0 = head * static_cast<int64_t>(args.fine_blocks) * kReps;
+            int issued = 0;
+            for (int t = 0; t < tiles; ++t) {
+                const int st = t % kLseStages;
+                const int use = t / kLseStages;
+                if (use > 0 && !tc::mbar_wait(bar(kLseBarBEmpty + st), (use - 1) & 1, abort_flag, kLseWaitLimit))
+                    break;
+                issued = t + 1;
+                tc::mbar_arrive_expect_tx(bar(kLseBarBFull + st), kLseStageBytes);
+                const int32_t y = static_cast<int32_t>(key0 + static_cast<int64_t>(t) * kLseTileKeys);
+                const uint32_t dst = base + kLseOffB + st * kLseStageBytes;
+                tc::tma_load_2d(dst, &maps.keys, 0, y, bar(kLseBarBFull + st));
+                tc::tma_load_2d(dst + kLseSlabB, &maps.keys, 64, y, bar(kLseBarBFull + st));
             }
-            // Lane (g, t) holds rows g / g+8 of KV4 blocks 8*grp + t and 8*grp + t + 4.
-#pragma unroll
-            for (int r = 0; r < 2; ++r) {
-#pragma unroll
-                for (int nt = 0; nt < 2; ++nt) {
-                    const int local = grp * 8 + nt * 4 + t;
-                    const int block = tile * kLseTileBlocks + local;
-                    const half stored = __float2half_rn(
-                        pair_lse(acc[nt][2 * r] + 1.0f, acc[nt][2 * r + 1] + 1.0f));
-                    staging[(g + 8 * r) * kLseStagingStride + local] = stored;
-                    if (block < fine_blocks) accumulate_lse(maximum[r], denominator[r], __half2float(stored));
+            // Drain: every tile issued above has landed before the CTA may exit.
+            for (int st = 0; st < kLseStages && st < issued; ++st) {
+                const int last_use = (issued - 1 - st) / kLseStages;
+                tc::mbar_wait(bar(kLseBarBFull + st), last_use & 1, abort_flag, kLseWaitLimit, false);
+            }
+            tc::mbar_wait(bar(kLseBarAFull), 0, abort_flag, kLseWaitLimit, false);
+        }
+        __syncwarp();
+    } else if (warp == kLseMmaWarp) {
+        if (lane == 0) {
+            bool ok = tc::mbar_wait(bar(kLseBarAFull), 0, abort_flag, kLseWaitLimit);
+            for (int t = 0; ok && t < tiles; ++t) {
+                const int st = t % kLseStages;
+                const int b = t & 1;
+                if (!tc::mbar_wait(bar(kLseBarBFull + st), (t / kLseStages) & 1, abort_flag, kLseWaitLimit) ||
+                    (t >= 2 && !tc::mbar_wait(bar(kLseBarTEmpty + b), ((t >> 1) - 1) & 1, abort_flag,
+                                              kLseWaitLimit))) {
+                    ok = false;
+                    break;
                 }
-            }
-        }
-        __syncwarp();
-        // Write the warp's 16 x 64 fp16 tile: 16 rows x 8 chunks of 16 bytes.
-        const int block0 = tile * kLseTileBlocks;
+                tc::fence_after_sync();
+                const uint32_t b_base = base + kLseOffB + st * kLseStageBytes;
 #pragma unroll
-        for (int it = 0; it < 4; ++it) {
-            const int idx = it * 32 + lane;
-            const int rr = idx >> 3;
-            const int c = idx & 7;
-            const int64_t m = m0 + rr;
-            if (m >= head_rows) continue;
-            half* dst = lse + (head * head_rows + m) * ld + block0 + c * 8;
-            const half* s = staging + rr * kLseStagingStride + c * 8;
-            const int avail = fine_blocks - (block0 + c * 8);
-            if (vec_store && avail >= 8) {
-                *reinterpret_cast<uint4*>(dst) = *reinterpret_cast<const uint4*>(s);
-            } else {
-                for (int e = 0; e < 8 && e < avail; ++e) dst[e] = s[e];
+                for (int j = 0; j < 8; ++j) {
+                    // 16 dims per step inside a 64-dim slab: advance the start by 32 bytes.
+                    const uint64_t adesc =
+                        tc::smem_desc(base + kLseOffA + (j >> 2) * kLseSlabA + (j & 3) * 32, 16, 1024, tc::kSwizzle128B);
+                    const uint64_t bdesc =
+                        tc::smem_desc(b_base + (j >> 2) * kLseSlabB + (j & 3) * 32, 16, 1024, tc::kSwizzle128B);
+                    tc::mma_ss(tmem + b * kLseTileKeys, adesc, bdesc, kLseIdesc, j > 0 ? 1u : 0u);
+                }
+                tc::mma_commit(bar(kLseBarBEmpty + st));
+                tc::mma_commit(bar(kLseBarTFull + b));
             }
+            // Drain: every MMA issued above has completed before TMEM is freed.
+            tc::mma_commit(bar(kLseBarDrain));
+            tc::mbar_wait(bar(kLseBarDrain), 0, abort_flag, kLseWaitLimit, false);
         }
         __syncwarp();
+    } else {
+        const int m = threadIdx.x;  // TMEM lane = centroid row row0 + m
+        const int64_t row = row0 + m;
+        const bool valid = row < args.head_rows;
+        const int64_t global_row = head * args.head_rows + row;
+        half* out = args.lse + global_row * args.ld;
+        const uint32_t lane_base = tmem + (static_cast<uint32_t>(warp * 32) << 16);
+        float mx[4] = {-FLT_MAX, -FLT_MAX, -FLT_MAX, -FLT_MAX};
+        float dn[4] = {0.f, 0.f, 0.f, 0.f};
+        bool ok = true;
+        for (int t = 0; t < tiles; ++t) {
+            const int b = t & 1;
+            if (!tc::mbar_wait_warp(bar(kLseBarTFull + b), (t >> 1) & 1, abort_flag, kLseWaitLimit)) {
+                ok = false;
+                break;
+            }
+            tc::fence_after_sync();
+            uint32_t lo[32], hi[32];
+            tc::tmem_ld32(lane_base + b * kLseTileKeys, lo);
+            tc::tmem_ld32(lane_base + b * kLseTileKeys + 32, hi);
+            tc::tmem_wait_ld();
+            tc::tmem_reg_fence(lo);
+            tc::tmem_reg_fence(hi);
+            tc::fence_before_sync();
+            tc::mbar_arrive(bar(kLseBarTEmpty + b));
+            const int j0 = t * kLseTileBlocks;
+            if (j0 + kLseTileBlocks <= args.fine_blocks) {
+                lse_tile<true>(lo, j0, args.fine_blocks, out, valid, args.vector_rows, mx, dn);
+                lse_tile<true>(hi, j0 + 16, args.fine_blocks, out, valid, args.vector_rows, mx, dn);
+            } else {
+                lse_tile<false>(lo, j0, args.fine_blocks, out, valid, args.vector_rows, mx, dn);
+                lse_tile<false>(hi, j0 + 16, args.fine_blocks, out, valid, args.vector_rows, mx, dn);
+            }
+        }
+        if (ok && valid) {
+            // (c0 + c1) + (c2 + c3), each merge in the reference's operand order.
+            float m01 = mx[0], d01 = dn[0];
+            combine_lse(m01, d01, mx[1], dn[1]);
+            float m23 = mx[2], d23 = dn[2];
+            combine_lse(m23, d23, mx[3], dn[3]);
+            combine_lse(m01, d01, m23, d23);
+            args.lse_max[global_row] = m01;
+            args.lse_den[global_row] = d01;
+        }
     }
 
-    // Merge the four lane classes: (c0+c1)+(c2+c3) (csrc/ibcs.cu:468-477).
-#pragma unroll
-    for (int mask = 1; mask <= 2; mask <<= 1) {
-#pragma unroll
-        for (int r = 0; r < 2; ++r) {
-            combine_lse(maximum[r], denominator[r], __shfl_xor_sync(0xffffffffu, maximum[r], mask),
-                        __shfl_xor_sync(0xffffffffu, denominator[r], mask));
-        }
+    tc::fence_before_sync();
+    __syncthreads();
+    if (warp == kLseLoadWarp) {
+        tc::fence_after_sync();
+        tc::tmem_dealloc(tmem, kLseTmemColumns);
     }
-    if (t == 0) {
-#pragma unroll
-        for (int r = 0; r < 2; ++r) {
-            const int64_t m = m0 + g + 8 * r;
-            if (m < head_rows) {
-                lse_max[head * head_rows + m] = maximum[r];
-                lse_den[head * head_rows + m] = denominator[r];
-            }
-        }
-    }
+    if (threadIdx.x == 0 && *abort_flag) raise_device_error(args.error, ABX_ERR_DEVICE_TIMEOUT);
 }
 
 // ---------------------------------------------------------------------------
-// Population-weighted mixture (standalone; build_plan fuses it into SIP).
+// Population-weighted mixture (csrc/ibcs.cu:495-538): the third pass of IBCS.
 // ---------------------------------------------------------------------------
 
 constexpr int kMixThreads = 256;
-constexpr int kMixPerThread = 4;  // scores per thread; all 32 fp16 loads are issued before the math
+constexpr int kMixPerThread = 8;  // consecutive KV4 blocks per thread: one 16-byte load per centroid
 
-// grid (rows, ceil(F / (256 * 4))): a CTA covers 1024 consecutive KV4 blocks of one row.
+// grid (rows, ceil(F / 2048)): a CTA covers 2048 consecutive KV4 blocks of one row.
+// kVector: every LSE row starts on a 16-byte boundary (ld % 8 == 0, aligned base);
+// loads then cover [j0, j0 + 8) and may read the row's padding past F.
+template <bool kVector>
 __global__ __launch_bounds__(kMixThreads) void mix_kernel(const half* __restrict__ lse, int64_t ld,
                                                           const float* __restrict__ populations,
                                                           const float* __restrict__ lse_max,
@@ -416,28 +552,43 @@ __global__ __launch_bounds__(kMixThreads) void mix_kernel(const half* __restrict
         row_weight[threadIdx.x] = populations[row * kCentroids + threadIdx.x];
     }
     __syncthreads();
+    const int j0 = (blockIdx.y * kMixThreads + threadIdx.x) * kMixPerThread;
+    if (j0 >= fine_blocks) return;
+    const half* base = lse + row * kCentroids * ld + j0;
+    half value[kCentroids][kMixPerThread];
+    if constexpr (kVector) {
+#pragma unroll
+        for (int c = 0; c < kCentroids; ++c)
+            *reinterpret_cast<uint4*>(value[c]) = __ldg(reinterpret_cast<const uint4*>(base + c * ld));
+    } else {
+        const int last = fine_blocks - 1 - j0;
+#pragma unroll
+        for (int c = 0; c < kCentroids; ++c)
+#pragma unroll
+            for (int e = 0; e < kMixPerThread; ++e) value[c][e] = base[c * ld + min(e, last)];
+    }
     float total_weight = 0.0f;
 #pragma unroll
     for (int c = 0; c < kCentroids; ++c) total_weight += row_weight[c];
-    const int j0 = blockIdx.y * (kMixThreads * kMixPerThread) + threadIdx.x;
-    const half* base = lse + row * kCentroids * ld;
-    half value[kMixPerThread][kCentroids];
+    float out[kMixPerThread];
 #pragma unroll
-    for (int u = 0; u < kMixPerThread; ++u) {
-        const int j = min(j0 + u * kMixThreads, fine_blocks - 1);
-#pragma unroll
-        for (int c = 0; c < kCentroids; ++c) value[u][c] = base[c * ld + j];
-    }
-#pragma unroll
-    for (int u = 0; u < kMixPerThread; ++u) {
-        const int j = j0 + u * kMixThreads;
+    for (int e = 0; e < kMixPerThread; ++e) {
         float score = 0.0f;
 #pragma unroll
         for (int c = 0; c < kCentroids; ++c) {
-            const float probability = exp2f(__half2float(value[u][c]) - row_max[c]) / row_den[c];
+            const float probability = exp2f(__half2float(value[c][e]) - row_max[c]) / row_den[c];
             score += row_weight[c] * probability;
         }
-        if (j < fine_blocks) scores[row * fine_blocks + j] = score / total_weight;
+        out[e] = score / total_weight;
+    }
+    float* dst = scores + row * fine_blocks + j0;
+    if (j0 + kMixPerThread <= fine_blocks && (reinterpret_cast<uintptr_t>(dst) & 15) == 0) {
+        reinterpret_cast<float4*>(dst)[0] = make_float4(out[0], out[1], out[2], out[3]);
+        reinterpret_cast<float4*>(dst)[1] = make_float4(out[4], out[5], out[6], out[7]);
+    } else {
+#pragma unroll
+        for (int e = 0; e < kMixPerThread; ++e)
+            if (j0 + e < fine_blocks) dst[e] = out[e];
     }
 }
 
@@ -463,21 +614,31 @@ cudaError_t launch_pool(const bf16* k, int64_t bh, int64_t seq, bf16* pooled, cu
     return cudaGetLastError();
 }
 
-size_t lse_smem_bytes() {
-    return 2 * kLseStageChunks * sizeof(uint4) + kLseWarps * kLseStagingHalfs * sizeof(half);
-}
+size_t lse_smem_bytes() { return kLseSmemBytes; }
 
 cudaError_t launch_lse(const bf16* scaled, const bf16* pooled, int64_t bh, int64_t qb,
                        int64_t fine_blocks, int64_t ld, half* lse, float* lse_max, float* lse_den,
                        cudaStream_t stream) {
-    const size_t smem = lse_smem_bytes();
-    cudaError_t err = cudaFuncSetAttribute(lse_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                           static_cast<int>(smem));
+    LseMaps maps{};
+    cudaError_t err;
+    const int64_t head_rows = qb * kCentroids;
+    if ((err = encode_rows(&maps.centroids, scaled, bh * head_rows, kLseRows)) != cudaSuccess) return err;
+    if ((err = encode_rows(&maps.keys, pooled, bh * fine_blocks * kReps, kLseTileKeys)) != cudaSuccess) return err;
+    LseArgs args{};
+    args.head_rows = head_rows;
+    args.ld = ld;
+    args.fine_blocks = static_cast<int>(fine_blocks);
+    args.tiles = static_cast<int>(ceil_div(fine_blocks, kLseTileBlocks));
+    args.lse = lse;
+    args.lse_max = lse_max;
+    args.lse_den = lse_den;
+    args.error = device_error_word();
+    args.vector_rows = ld % 8 == 0 && (reinterpret_cast<uintptr_t>(lse) & 15) == 0;
+    err = cudaFuncSetAttribute(lse_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               static_cast<int>(kLseSmemBytes));
     if (err != cudaSuccess) return err;
-    const dim3 grid(static_cast<unsigned>(ceil_div(qb * kCentroids, kLseRowsPerCta)),
-                    static_cast<unsigned>(bh));
-    lse_kernel<<<grid, kLseThreads, smem, stream>>>(scaled, pooled, qb, static_cast<int>(fine_blocks),
-                                                    ld, lse, lse_max, lse_den);
+    const dim3 grid(static_cast<unsigned>(ceil_div(head_rows, kLseRows)), static_cast<unsigned>(bh));
+    lse_kernel<<<grid, kLseThreads, kLseSmemBytes, stream>>>(maps, args);
     return cudaGetLastError();
 }
 
@@ -486,8 +647,13 @@ cudaError_t launch_mix(const half* lse, int64_t ld, const float* populations, co
                        cudaStream_t stream) {
     const dim3 grid(static_cast<unsigned>(rows),
                     static_cast<unsigned>(ceil_div(fine_blocks, kMixThreads * kMixPerThread)));
-    mix_kernel<<<grid, kMixThreads, 0, stream>>>(lse, ld, populations, lse_max, lse_den,
-                                                 static_cast<int>(fine_blocks), scores);
+    const bool vector = ld % 8 == 0 && (reinterpret_cast<uintptr_t>(lse) & 15) == 0;
+    if (vector)
+        mix_kernel<true><<<grid, kMixThreads, 0, stream>>>(lse, ld, populations, lse_max, lse_den,
+                                                           static_cast<int>(fine_blocks), scores);
+    else
+        mix_kernel<false><<<grid, kMixThreads, 0, stream>>>(lse, ld, populations, lse_max, lse_den,
+                                                            static_cast<int>(fine_blocks), scores);
     return cudaGetLastError();
 }
 

@@ -37,6 +37,7 @@
 #include "common.cuh"
 #include "ibcs.cuh"
 #include "tcgen05.cuh"
+#include "tma_host.cuh"
 
 #include <cfloat>
 #include <mutex>
@@ -482,34 +483,6 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const PrefillArgs 
 }
 
 }  // namespace
-
-// cuTensorMapEncodeTiled through the runtime's driver entry point (no libcuda link).
-static PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
-    static std::once_flag once;
-    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
-    std::call_once(once, [] {
-        void* ptr = nullptr;
-        cudaDriverEntryPointQueryResult status;
-        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &status) == cudaSuccess &&
-            status == cudaDriverEntryPointSuccess)
-            fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(ptr);
-    });
-    return fn;
-}
-
-// [rows, 128] bf16 row-major, box = 64 columns x box_rows rows, 128-byte swizzle.
-static cudaError_t encode_rows(CUtensorMap* map, const void* base, int64_t rows, uint32_t box_rows) {
-    auto encode = tensor_map_encoder();
-    if (encode == nullptr) return cudaErrorNotSupported;
-    const cuuint64_t dims[2] = {static_cast<cuuint64_t>(kHeadDim), static_cast<cuuint64_t>(rows)};
-    const cuuint64_t strides[1] = {static_cast<cuuint64_t>(kHeadDim) * 2};
-    const cuuint32_t box[2] = {64, box_rows};
-    const cuuint32_t elem_strides[2] = {1, 1};
-    const CUresult r = encode(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box,
-                              elem_strides, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
-                              CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-    return r == CUDA_SUCCESS ? cudaSuccess : cudaErrorInvalidValue;
-}
 
 cudaError_t launch_prefill(const bf16* q, const bf16* k, const bf16* v, int64_t bh, int64_t seq,
                            const int32_t* ids, const float* log_weights, int64_t samples,

@@ -46,22 +46,33 @@ union Scratch {
     MassScan::TempStorage mass;
 };
 
-// Dynamic shared memory: the bucket prefix (doubles) then the masses (floats).
+// Dynamic shared memory: the bucket prefix (doubles) then the masses (floats,
+// starting on a 16-byte boundary for the float4 chunk sweeps).
 // CUB's temporaries live at the start of the prefix region: every block
 // reduction and scan finishes before the first prefix entry is written, and
 // keeping them out of static shared memory lets two rows share an SM at the
 // Wan2.1 shape (F = 18,900).
 __host__ __device__ constexpr size_t sip_prefix_region(int64_t population) {
     const size_t prefix = static_cast<size_t>((population + kSipBucket - 1) / kSipBucket + 1) * sizeof(double);
-    return prefix > sizeof(Scratch) ? prefix : (sizeof(Scratch) + 15) / 16 * 16;
+    const size_t region = prefix > sizeof(Scratch) ? prefix : sizeof(Scratch);
+    return (region + 15) / 16 * 16;
 }
+
+constexpr int kLoadUnroll = 8;  // score loads in flight per thread
+constexpr int kMarkUnroll = 4;  // masses per thread per step of the marking sweep
+constexpr int kDrawGroup = 4;   // draws per thread searched in lockstep
+
+// mass_j = v_j * scale for a residual unit (v_j > 0), 0 for a certain one; the
+// expression has the reference's shape (csrc/sip.cu:127,140), so the multiply
+// is not fused into the running sum.
+#define SIP_MASS(f, s) ((f) > 0.f ? static_cast<double>(f) * (s) : 0.)
 
 template <class Source>
 __global__ __launch_bounds__(kSipThreads) void sip_kernel(Source source, const float* __restrict__ offsets,
                                                           int32_t* __restrict__ sampled,
                                                           float* __restrict__ weights, int population,
                                                           int samples) {
-    extern __shared__ double prefix[];
+    extern __shared__ __align__(16) double prefix[];
     Scratch& scratch = *reinterpret_cast<Scratch*>(prefix);
     __shared__ double scale;
     __shared__ int certain;
@@ -76,26 +87,44 @@ __global__ __launch_bounds__(kSipThreads) void sip_kernel(Source source, const f
     int32_t* out_ids = sampled + row * samples;
     float* out_logs = weights + row * samples;
 
+    // v_j = max(score_j, 1e-30f) (csrc/sip.cu:58-59), fused with the first
+    // iteration's partial sums. Every v_j is positive and its double is above
+    // 1e-30, so the reference's `v > 0` test and fmax(v, 1e-30) are identities
+    // here; the sums visit j = tid, tid + 256, ... in order as there.
     source.prepare(row);
-    for (int j = tid; j < population; j += kSipThreads) values[j] = fmaxf(source.score(row, j), 1e-30f);
+    double local_sum = 0.;
+    double local_max = 0.;
+    {
+        int j = tid;
+        for (; j + (kLoadUnroll - 1) * kSipThreads < population; j += kLoadUnroll * kSipThreads) {
+            float f[kLoadUnroll];
+#pragma unroll
+            for (int u = 0; u < kLoadUnroll; ++u) f[u] = fmaxf(source.score(row, j + u * kSipThreads), 1e-30f);
+#pragma unroll
+            for (int u = 0; u < kLoadUnroll; ++u) {
+                values[j + u * kSipThreads] = f[u];
+                const double value = static_cast<double>(f[u]);
+                local_sum += value;
+                local_max = fmax(local_max, value);
+            }
+        }
+        for (; j < population; j += kSipThreads) {
+            const float f = fmaxf(source.score(row, j), 1e-30f);
+            values[j] = f;
+            const double value = static_cast<double>(f);
+            local_sum += value;
+            local_max = fmax(local_max, value);
+        }
+    }
     if (tid == 0) certain = 0;
-    __syncthreads();
 
     // Iterative certainty: mark every unit whose inclusion probability reaches 1
     // (negated in place) until the residual budget is stable (csrc/sip.cu:62-96).
     // The reference re-sums the uncertain masses after each marking pass; the
     // units a marking pass leaves unmarked are exactly the terms of that sum,
     // visited in the same per-thread order, so the marking pass accumulates the
-    // next partial sums itself and each iteration is one pass instead of two.
-    double local_sum = 0.;
-    double local_max = 0.;
-    for (int j = tid; j < population; j += kSipThreads) {
-        if (values[j] > 0.f) {
-            const double value = fmax(static_cast<double>(values[j]), 1e-30);
-            local_sum += value;
-            local_max = fmax(local_max, value);
-        }
-    }
+    // next partial sums itself (adding +0.0 for a skipped unit, which leaves a
+    // non-negative sum unchanged) and each iteration is one pass instead of two.
     do {
         const SumMax total = Reduce(scratch.reduce).Reduce(SumMax{local_sum, local_max}, SumMaxOp{});
         if (tid == 0) {
@@ -105,20 +134,37 @@ __global__ __launch_bounds__(kSipThreads) void sip_kernel(Source source, const f
         }
         __syncthreads();
         if (marking) {
+            const double s = scale;
             int count = 0;
             local_sum = 0.;
             local_max = 0.;
-            for (int j = tid; j < population; j += kSipThreads) {
-                if (values[j] > 0.f) {
-                    const double value = fmax(static_cast<double>(values[j]), 1e-30);
-                    if (value * scale >= 1.) {
-                        values[j] = -values[j];
-                        ++count;
-                    } else {
-                        local_sum += value;
-                        local_max = fmax(local_max, value);
-                    }
+            int j = tid;
+            for (; j + (kMarkUnroll - 1) * kSipThreads < population; j += kMarkUnroll * kSipThreads) {
+                float f[kMarkUnroll];
+#pragma unroll
+                for (int u = 0; u < kMarkUnroll; ++u) f[u] = values[j + u * kSipThreads];
+#pragma unroll
+                for (int u = 0; u < kMarkUnroll; ++u) {
+                    const bool live = f[u] > 0.f;
+                    const double value = static_cast<double>(f[u]);
+                    const bool mark = live && value * s >= 1.;
+                    if (mark) values[j + u * kSipThreads] = -f[u];
+                    count += mark;
+                    const double kept = live && !mark ? value : 0.;
+                    local_sum += kept;
+                    local_max = fmax(local_max, kept);
                 }
+            }
+            for (; j < population; j += kSipThreads) {
+                const float f = values[j];
+                const bool live = f > 0.f;
+                const double value = static_cast<double>(f);
+                const bool mark = live && value * s >= 1.;
+                if (mark) values[j] = -f;
+                count += mark;
+                const double kept = live && !mark ? value : 0.;
+                local_sum += kept;
+                local_max = fmax(local_max, kept);
             }
             atomicAdd(&added, count);
         }
@@ -127,25 +173,43 @@ __global__ __launch_bounds__(kSipThreads) void sip_kernel(Source source, const f
         __syncthreads();
     } while (added != 0);
 
-    // Contiguous chunks of whole buckets per thread (csrc/sip.cu:98-106).
+    // Contiguous chunks of whole buckets per thread (csrc/sip.cu:98-106). The
+    // chunk length is a multiple of 4 floats, so a chunk is a run of float4s
+    // (conflict-free across a quarter warp) plus, in the last chunk, a tail.
     const int chunk = ((buckets + kSipThreads - 1) / kSipThreads) * kSipBucket;
     const int begin = tid * chunk;
     const int end = min(begin + chunk, population);
+    const int quads = end > begin ? (end - begin) / 4 : 0;
+    const int tail = begin + 4 * quads;
+    const float4* chunk4 = reinterpret_cast<const float4*>(values + begin);
     if (tid == 0) {
         int last = population - 1;
         while (last >= 0 && values[last] <= 0.) --last;
         last_residual = last;
     }
     __syncthreads();
+    const double s = scale;
 
     // Certain units first, ascending, log-weight 0 (csrc/sip.cu:108-124).
     if (certain != 0) {
         int count = 0;
-        for (int j = begin; j < end; ++j) count += values[j] < 0.f;
+        for (int i = 0; i < quads; ++i) {
+            const float4 f = chunk4[i];
+            count += (f.x < 0.f) + (f.y < 0.f) + (f.z < 0.f) + (f.w < 0.f);
+        }
+        for (int j = tail; j < end; ++j) count += values[j] < 0.f;
         int rank = 0;
         CountScan(scratch.count).InclusiveSum(count, rank);
         int slot = rank - count;
-        for (int j = begin; j < end; ++j) {
+        for (int i = 0; i < quads; ++i) {
+            const float4 f = chunk4[i];
+            const int j = begin + 4 * i;
+            if (f.x < 0.f) { out_ids[slot] = j; out_logs[slot++] = 0.f; }
+            if (f.y < 0.f) { out_ids[slot] = j + 1; out_logs[slot++] = 0.f; }
+            if (f.z < 0.f) { out_ids[slot] = j + 2; out_logs[slot++] = 0.f; }
+            if (f.w < 0.f) { out_ids[slot] = j + 3; out_logs[slot++] = 0.f; }
+        }
+        for (int j = tail; j < end; ++j) {
             if (values[j] < 0.f) {
                 out_ids[slot] = j;
                 out_logs[slot++] = 0.f;
@@ -156,48 +220,94 @@ __global__ __launch_bounds__(kSipThreads) void sip_kernel(Source source, const f
 
     // Bucketed prefix of the residual masses (csrc/sip.cu:126-142).
     double chunk_mass = 0.;
-    for (int j = begin; j < end; ++j)
-        chunk_mass += values[j] > 0.f ? static_cast<double>(values[j]) * scale : 0.;
+    for (int i = 0; i < quads; ++i) {
+        const float4 f = chunk4[i];
+        chunk_mass += SIP_MASS(f.x, s);
+        chunk_mass += SIP_MASS(f.y, s);
+        chunk_mass += SIP_MASS(f.z, s);
+        chunk_mass += SIP_MASS(f.w, s);
+    }
+    for (int j = tail; j < end; ++j) chunk_mass += SIP_MASS(values[j], s);
     double cumulative = 0.;
     MassScan(scratch.mass).ExclusiveSum(chunk_mass, cumulative);
     __syncthreads();  // the scan's temporaries overlap the prefix written below
     const int residuals = samples - certain;
+    const int last = last_residual;
     if (tid == 0) prefix[buckets] = residuals;
-    for (int j = begin; j < end; ++j) {
-        if (j % kSipBucket == 0) prefix[j / kSipBucket] = j > last_residual ? residuals : cumulative;
-        cumulative += values[j] > 0.f ? static_cast<double>(values[j]) * scale : 0.;
+    for (int i = 0; i < quads; ++i) {
+        const float4 f = chunk4[i];
+        const int j = begin + 4 * i;  // a bucket start
+        prefix[j / kSipBucket] = j > last ? residuals : cumulative;
+        cumulative += SIP_MASS(f.x, s);
+        cumulative += SIP_MASS(f.y, s);
+        cumulative += SIP_MASS(f.z, s);
+        cumulative += SIP_MASS(f.w, s);
+    }
+    for (int j = tail; j < end; ++j) {
+        if (j % kSipBucket == 0) prefix[j / kSipBucket] = j > last ? residuals : cumulative;
+        cumulative += SIP_MASS(values[j], s);
     }
     __syncthreads();
 
     // Systematic draws at u + k: bucket search, then a walk of at most four
     // masses; the last residual closes roundoff escapes (csrc/sip.cu:144-166).
+    // A thread's draws (slots tid, tid + 256, ...) are searched in lockstep
+    // groups for instruction-level parallelism; each draw's steps are the
+    // reference's.
     const double offset = static_cast<double>(offsets[row]);
-    for (int slot = tid; slot < residuals; slot += kSipThreads) {
-        const double threshold = offset + slot;
-        int lower = 0, upper = buckets;
-        while (lower < upper) {
-            const int middle = (lower + upper + 1) / 2;
-            if (prefix[middle] <= threshold) lower = middle;
-            else upper = middle - 1;
+    for (int first = tid; first < residuals; first += kDrawGroup * kSipThreads) {
+        double threshold[kDrawGroup];
+        int lower[kDrawGroup], upper[kDrawGroup];
+        bool busy = false;
+#pragma unroll
+        for (int k = 0; k < kDrawGroup; ++k) {
+            const int slot = first + k * kSipThreads;
+            threshold[k] = offset + slot;
+            lower[k] = 0;
+            upper[k] = slot < residuals ? buckets : 0;
+            busy |= lower[k] < upper[k];
         }
-        const int bucket = min(lower, buckets - 1);
-        double mass = prefix[bucket];
-        int selected = last_residual;
-        const int stop = min((bucket + 1) * kSipBucket, population);
-        for (int j = bucket * kSipBucket; j < stop; ++j) {
-            if (values[j] <= 0.f) continue;
-            selected = j;
-            mass += static_cast<double>(values[j]) * scale;
-            if (mass > threshold) break;
+        while (busy) {
+            busy = false;
+#pragma unroll
+            for (int k = 0; k < kDrawGroup; ++k) {
+                if (lower[k] < upper[k]) {
+                    const int middle = (lower[k] + upper[k] + 1) / 2;
+                    if (prefix[middle] <= threshold[k]) lower[k] = middle;
+                    else upper[k] = middle - 1;
+                    busy |= lower[k] < upper[k];
+                }
+            }
         }
-        // The weight uses the unclamped score; `values` holds max(score, 1e-30f),
-        // which equals it unless the clamp was active.
-        const float kept = values[selected];
-        const float raw = kept == 1e-30f ? source.score(row, selected) : kept;
-        out_ids[certain + slot] = selected;
-        out_logs[certain + slot] = static_cast<float>(-log2(fmax(static_cast<double>(raw), 1e-30) * scale));
+        int selected[kDrawGroup];
+#pragma unroll
+        for (int k = 0; k < kDrawGroup; ++k) {
+            const int bucket = min(lower[k], buckets - 1);
+            double mass = prefix[bucket];
+            selected[k] = last;
+            const int stop = min((bucket + 1) * kSipBucket, population);
+            for (int j = bucket * kSipBucket; j < stop; ++j) {
+                if (values[j] <= 0.f) continue;
+                selected[k] = j;
+                mass += static_cast<double>(values[j]) * scale;
+                if (mass > threshold[k]) break;
+            }
+        }
+#pragma unroll
+        for (int k = 0; k < kDrawGroup; ++k) {
+            const int slot = first + k * kSipThreads;
+            if (slot >= residuals) break;
+            // The weight uses the unclamped score; `values` holds max(score, 1e-30f),
+            // which equals it unless the clamp was active.
+            const float kept = values[selected[k]];
+            const float raw = kept == 1e-30f ? source.score(row, selected[k]) : kept;
+            out_ids[certain + slot] = selected[k];
+            out_logs[certain + slot] = static_cast<float>(-log2(fmax(static_cast<double>(raw), 1e-30) * scale));
+        }
     }
 }
+
+#undef SIP_MASS
 
 }  // namespace
 
