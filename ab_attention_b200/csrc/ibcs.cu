@@ -247,24 +247,29 @@ __global__ __launch_bounds__(256) void pool_kernel(const bf16* __restrict__ k, i
 //              four running (max, den) chains by block index mod 4 (the
 //              reference's four lane classes, csrc/ibcs.cu:329-335,454-462),
 //              merged at the end as (c0 + c1) + (c2 + c3) (:468-477).
-//   warp 4     TMA: the 32 KB centroid tile once, then 16 KB key tiles into a
-//              3-stage ring; allocates and frees TMEM.
-//   warp 5     one thread issues the MMAs into two TMEM buffers.
+//   warp 4     allocates and frees TMEM; one thread loads the 32 KB centroid
+//              tile once and 16 KB key tiles into a 3-stage ring (TMA), and
+//              issues the MMAs into two TMEM buffers.
+// Each epilogue warp stages its 32 rows x 32 blocks of fp16 per tile in shared
+// memory (64-byte swizzle, double-buffered) and writes them with one TMA store:
+// 64-byte row segments instead of 32 scattered 16-byte stores per instruction.
 // ---------------------------------------------------------------------------
 
 constexpr int kLseRows = 128;                          // centroid rows per CTA = TMEM lanes
 constexpr int kLseTileBlocks = 32;                     // KV4 blocks per key tile
 constexpr int kLseTileKeys = kLseTileBlocks * kReps;  // 64 pooled rows = MMA N
 constexpr int kLseStages = 3;
-constexpr int kLseLoadWarp = 4;
-constexpr int kLseMmaWarp = 5;
-constexpr int kLseThreads = 6 * 32;
+constexpr int kLseCtlWarp = 4;  // TMEM allocation, TMA and MMA issue
+constexpr int kLseThreads = 5 * 32;
 constexpr uint32_t kLseSlabA = kLseRows * 128;      // 128 rows x 64 bf16
 constexpr uint32_t kLseSlabB = kLseTileKeys * 128;  // 64 rows x 64 bf16
 constexpr uint32_t kLseStageBytes = 2 * kLseSlabB;
 constexpr uint32_t kLseOffA = 0;
 constexpr uint32_t kLseOffB = 2 * kLseSlabA;
-constexpr uint32_t kLseOffBar = kLseOffB + kLseStages * kLseStageBytes;
+constexpr uint32_t kLseStageRowBytes = kLseTileBlocks * 2;                // 64 B of fp16 per row and tile
+constexpr uint32_t kLseOutBufBytes = 32 * kLseStageRowBytes;                // one warp's 32 rows
+constexpr uint32_t kLseOffOut = kLseOffB + kLseStages * kLseStageBytes;   // 4 warps x 2 buffers
+constexpr uint32_t kLseOffBar = kLseOffOut + 4 * 2 * kLseOutBufBytes;
 constexpr int kLseBarAFull = 0;
 constexpr int kLseBarBFull = 1;                            // kLseStages
 constexpr int kLseBarBEmpty = kLseBarBFull + kLseStages;  // kLseStages
@@ -282,6 +287,7 @@ constexpr uint64_t kLseWaitLimit = 400ull * 1000 * 1000;  // SM cycles per wait 
 struct LseMaps {
     CUtensorMap centroids;  // [bh * qb * 8, 128], box 64 x 128 rows
     CUtensorMap keys;       // [bh * F * 2, 128], box 64 x 64 rows
+    CUtensorMap out;        // fp16 [bh][qb * 8][ld] (F columns), box 32 x 32 rows (vector_rows only)
 };
 
 struct LseArgs {
@@ -305,15 +311,6 @@ __device__ __forceinline__ float unit_exp(float x) {
     return r;
 }
 
-// The reference's pair_lse (csrc/ibcs.cu:339-343):
-//   M = fmax(l, r); M + log2(fmax(2^(l - M) + 2^(r - M), 1e-20)).
-// The term of the operand equal to M is 2^(M - M) = unit_exp(M); the other is
-// 2^(-|l - r|) (l - r and r - l differ only in sign); the addition commutes.
-__device__ __forceinline__ float pair_lse(float left, float right) {
-    const float maximum = fmaxf(left, right);
-    return maximum + log2f(fmaxf(unit_exp(maximum) + exp2f(-fabsf(left - right)), 1.0e-20f));
-}
-
 // The reference's accumulate_lse (csrc/ibcs.cu:329-335):
 //   next = fmax(max, v); den = den * 2^(max - next) + 2^(v - next); max = next.
 // One exponent is next - next (ex2 = unit_exp(next)), the other -|max - v|;
@@ -334,36 +331,110 @@ __device__ __forceinline__ void combine_lse(float& maximum, float& denominator, 
     maximum = next;
 }
 
+// ---- packed f32x2 arithmetic (sm_100): two independent IEEE operations per
+// instruction, flushing subnormals like the --use_fast_math scalar forms ----
+__device__ __forceinline__ uint64_t pack2(float x, float y) {
+    uint64_t r;
+    asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(x), "f"(y));
+    return r;
+}
+__device__ __forceinline__ float2 unpack2(uint64_t v) {
+    float2 r;
+    asm("mov.b64 {%0, %1}, %2;" : "=f"(r.x), "=f"(r.y) : "l"(v));
+    return r;
+}
+__device__ __forceinline__ uint64_t add2(uint64_t a, uint64_t b) {
+    uint64_t d;
+    asm("add.rn.ftz.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+    return d;
+}
+__device__ __forceinline__ uint64_t sub2(uint64_t a, uint64_t b) {
+    uint64_t d;
+    asm("sub.rn.ftz.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+    return d;
+}
+__device__ __forceinline__ uint64_t fma2(uint64_t a, uint64_t b, uint64_t c) {
+    uint64_t d;
+    asm("fma.rn.ftz.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+    return d;
+}
+constexpr uint64_t kOnes2 = 0x3F8000003F800000ull;  // (1.0f, 1.0f)
+constexpr uint64_t kZeros2 = 0;
+
+// The reference's pair_lse (csrc/ibcs.cu:339-343) for two blocks A and B, from
+// their raw representative scores with its "+ 1" (log2 of the representative
+// size) applied first:
+//   M = fmax(l, r); M + log2(fmax(2^(l - M) + 2^(r - M), 1e-20)).
+// The term of the operand equal to M is 2^(M - M) = unit_exp(M); the other is
+// 2^(-|l - r|) (l - r and r - l differ only in sign); the addition commutes.
+__device__ __forceinline__ float2 pair_lse2(uint32_t a0, uint32_t a1, uint32_t b0, uint32_t b1) {
+    const float2 la = unpack2(add2((static_cast<uint64_t>(a1) << 32) | a0, kOnes2));  // (l_A, r_A)
+    const float2 lb = unpack2(add2((static_cast<uint64_t>(b1) << 32) | b0, kOnes2));
+    const uint64_t m = pack2(fmaxf(la.x, la.y), fmaxf(lb.x, lb.y));
+    const uint64_t e = pack2(exp2f(-fabsf(la.x - la.y)), exp2f(-fabsf(lb.x - lb.y)));
+    const float2 sum = unpack2(add2(fma2(m, kZeros2, kOnes2), e));  // unit_exp(M) + e
+    return unpack2(add2(m, pack2(log2f(fmaxf(sum.x, 1.0e-20f)), log2f(fmaxf(sum.y, 1.0e-20f)))));
+}
+
+// accumulate_lse on two chains at once: chain pair (max, den) and one value each.
+__device__ __forceinline__ void accumulate_lse2(uint64_t& mx, uint64_t& dn, uint64_t v) {
+    const float2 m = unpack2(mx);
+    const float2 x = unpack2(v);
+    const float n0 = fmaxf(m.x, x.x);
+    const float n1 = fmaxf(m.y, x.y);
+    const float2 d = unpack2(sub2(mx, v));
+    const float e0 = exp2f(-fabsf(d.x));
+    const float e1 = exp2f(-fabsf(d.y));
+    const uint64_t n = pack2(n0, n1);
+    const float2 u = unpack2(fma2(n, kZeros2, kOnes2));
+    const bool k0 = n0 == m.x;
+    const bool k1 = n1 == m.y;
+    dn = fma2(dn, pack2(k0 ? u.x : e0, k1 ? u.y : e1), pack2(k0 ? e0 : u.x, k1 ? e1 : u.y));
+    mx = n;
+}
+
 // One tile of a row: 32 KV4 blocks from 64 accumulators (block k = columns 2k,
-// 2k + 1: the two pooled representatives). kFull: all 32 blocks are < F.
-template <bool kFull>
+// 2k + 1: the two pooled representatives). kFull: all 32 blocks are < F. The
+// chains are held as pairs (c0, c1) and (c2, c3): mx[0..1], dn[0..1].
+// kTma: the row's 16-byte chunks go to its 64-byte staging row (chunk c at
+// c ^ ((lane >> 1) & 3), the 64-byte swizzle of the store's tensor map);
+// otherwise straight to the row in global memory (rows not 16-byte aligned).
+template <bool kFull, bool kTma>
 __device__ __forceinline__ void lse_tile(const uint32_t (&acc)[32], int j0, int fine_blocks, half* out,
-                                         bool store, bool vector_rows, float (&mx)[4], float (&dn)[4]) {
+                                         bool store, uint32_t stage_row, int chunk0, int swz,
+                                         uint64_t (&mx)[2], uint64_t (&dn)[2]) {
 #pragma unroll
     for (int q = 0; q < 2; ++q) {
         uint32_t packed[4];
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
             const int k = 8 * q + 2 * e;
-            const float p0 = pair_lse(__uint_as_float(acc[2 * k]) + 1.0f, __uint_as_float(acc[2 * k + 1]) + 1.0f);
-            const float p1 =
-                pair_lse(__uint_as_float(acc[2 * k + 2]) + 1.0f, __uint_as_float(acc[2 * k + 3]) + 1.0f);
+            const float2 p = pair_lse2(acc[2 * k], acc[2 * k + 1], acc[2 * k + 2], acc[2 * k + 3]);
             // One packed cvt.rn.f16x2 rounds both (the same round-to-nearest as a
             // scalar conversion); the rounded values are what the chains see.
-            const half2 h = __floats2half2_rn(p0, p1);
+            const half2 h = __floats2half2_rn(p.x, p.y);
             const float2 r = __half22float2(h);
-            const int j = j0 + k;       // j % 4 == 2 * (e & 1)
-            const int c = 2 * (e & 1);
-            if (kFull || j < fine_blocks) accumulate_lse(mx[c], dn[c], r.x);
-            if (kFull || j + 1 < fine_blocks) accumulate_lse(mx[c + 1], dn[c + 1], r.y);
+            const int j = j0 + k;  // j % 4 == 2 * (e & 1): chains (0, 1) or (2, 3)
+            const int c = e & 1;
+            if (kFull) {
+                accumulate_lse2(mx[c], dn[c], pack2(r.x, r.y));
+            } else {
+                float2 m2 = unpack2(mx[c]), d2 = unpack2(dn[c]);
+                if (j < fine_blocks) accumulate_lse(m2.x, d2.x, r.x);
+                if (j + 1 < fine_blocks) accumulate_lse(m2.y, d2.y, r.y);
+                mx[c] = pack2(m2.x, m2.y);
+                dn[c] = pack2(d2.x, d2.y);
+            }
             packed[e] = *reinterpret_cast<const uint32_t*>(&h);
         }
-        const int jb = j0 + 8 * q;
-        if (store && (kFull || jb < fine_blocks)) {
-            if (vector_rows) {
-                // jb < F and jb % 8 == 0, so [jb, jb + 8) lies inside the row's ld = round_up(F, 8).
-                *reinterpret_cast<uint4*>(out + jb) = make_uint4(packed[0], packed[1], packed[2], packed[3]);
-            } else {
+        if constexpr (kTma) {
+            const uint32_t dst = stage_row + (static_cast<uint32_t>((chunk0 + q) ^ swz) << 4);
+            asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};\n" ::"r"(dst), "r"(packed[0]), "r"(packed[1]),
+                         "r"(packed[2]), "r"(packed[3])
+                         : "memory");
+        } else {
+            const int jb = j0 + 8 * q;
+            if (store && (kFull || jb < fine_blocks)) {
                 const half* hv = reinterpret_cast<const half*>(packed);
 #pragma unroll
                 for (int i = 0; i < 8; ++i)
@@ -403,7 +474,7 @@ __global__ __launch_bounds__(kLseThreads, 2) void lse_kernel(const __grid_consta
         tc::mbar_init(bar(kLseBarDrain), 1);
         tc::mbar_init_fence();
     }
-    if (warp == kLseLoadWarp) {
+    if (warp == kLseCtlWarp) {
         tc::tmem_alloc(smem_addr(tmem_slot), kLseTmemColumns);
         tc::tmem_relinquish();
     }
@@ -412,43 +483,31 @@ __global__ __launch_bounds__(kLseThreads, 2) void lse_kernel(const __grid_consta
     tc::fence_after_sync();
     const uint32_t tmem = *tmem_slot;
 
-    if (warp == kLseLoadWarp) {
+    if (warp == kLseCtlWarp) {
         if (lane == 0) {
-            tc::mbar_arrive_expect_tx(bar(kLseBarAFull), 2 * kLseSlabA);
-            const int32_t ay = static_cast<int32_t>(head * args.head_rows + row0);
-            tc::tma_load_2d(base + kLseOffA, &maps.centroids, 0, ay, bar(kLseBarAFull));
-            tc::tma_load_2d(base + kLseOffA + kLseSlabA, &maps.centroids, 64, ay, bar(kLseBarAFull));
             const int64_t key0 = head * static_cast<int64_t>(args.fine_blocks) * kReps;
-            int issued = 0;
-            for (int t = 0; t < tiles; ++t) {
+            auto load = [&](int t) {
                 const int st = t % kLseStages;
-                const int use = t / kLseStages;
-                if (use > 0 && !tc::mbar_wait(bar(kLseBarBEmpty + st), (use - 1) & 1, abort_flag, kLseWaitLimit))
-                    break;
-                issued = t + 1;
                 tc::mbar_arrive_expect_tx(bar(kLseBarBFull + st), kLseStageBytes);
                 const int32_t y = static_cast<int32_t>(key0 + static_cast<int64_t>(t) * kLseTileKeys);
                 const uint32_t dst = base + kLseOffB + st * kLseStageBytes;
                 tc::tma_load_2d(dst, &maps.keys, 0, y, bar(kLseBarBFull + st));
                 tc::tma_load_2d(dst + kLseSlabB, &maps.keys, 64, y, bar(kLseBarBFull + st));
-            }
-            // Drain: every tile issued above has landed before the CTA may exit.
-            for (int st = 0; st < kLseStages && st < issued; ++st) {
-                const int last_use = (issued - 1 - st) / kLseStages;
-                tc::mbar_wait(bar(kLseBarBFull + st), last_use & 1, abort_flag, kLseWaitLimit, false);
-            }
-            tc::mbar_wait(bar(kLseBarAFull), 0, abort_flag, kLseWaitLimit, false);
-        }
-        __syncwarp();
-    } else if (warp == kLseMmaWarp) {
-        if (lane == 0) {
+            };
+            tc::mbar_arrive_expect_tx(bar(kLseBarAFull), 2 * kLseSlabA);
+            const int32_t ay = static_cast<int32_t>(head * args.head_rows + row0);
+            tc::tma_load_2d(base + kLseOffA, &maps.centroids, 0, ay, bar(kLseBarAFull));
+            tc::tma_load_2d(base + kLseOffA + kLseSlabA, &maps.centroids, 64, ay, bar(kLseBarAFull));
+            int issued = 0;
+            for (; issued < kLseStages && issued < tiles; ++issued) load(issued);
             bool ok = tc::mbar_wait(bar(kLseBarAFull), 0, abort_flag, kLseWaitLimit);
             for (int t = 0; ok && t < tiles; ++t) {
                 const int st = t % kLseStages;
                 const int b = t & 1;
-                if (!tc::mbar_wait(bar(kLseBarBFull + st), (t / kLseStages) & 1, abort_flag, kLseWaitLimit) ||
+                if (!tc::mbar_wait(bar(kLseBarBFull + st), (t / kLseStages) & 1, abort_flag, kLseWaitLimit, true,
+                                   tc::kLongWaitHintNs) ||
                     (t >= 2 && !tc::mbar_wait(bar(kLseBarTEmpty + b), ((t >> 1) - 1) & 1, abort_flag,
-                                              kLseWaitLimit))) {
+                                              kLseWaitLimit, true, tc::kLongWaitHintNs))) {
                     ok = false;
                     break;
                 }
@@ -465,10 +524,27 @@ __global__ __launch_bounds__(kLseThreads, 2) void lse_kernel(const __grid_consta
                 }
                 tc::mma_commit(bar(kLseBarBEmpty + st));
                 tc::mma_commit(bar(kLseBarTFull + b));
+                // Refill the stage of tile t - 1 (its MMAs were queued before this
+                // tile's, so the tensor pipe stays busy meanwhile).
+                if (t >= 1 && issued < tiles) {
+                    const int prev = t - 1;
+                    if (!tc::mbar_wait(bar(kLseBarBEmpty + prev % kLseStages), (prev / kLseStages) & 1, abort_flag,
+                                       kLseWaitLimit, true, tc::kLongWaitHintNs)) {
+                        ok = false;
+                        break;
+                    }
+                    load(issued++);
+                }
             }
-            // Drain: every MMA issued above has completed before TMEM is freed.
+            // Drain: every MMA issued above has completed before TMEM is freed,
+            // and every key tile issued has landed before the CTA may exit.
             tc::mma_commit(bar(kLseBarDrain));
             tc::mbar_wait(bar(kLseBarDrain), 0, abort_flag, kLseWaitLimit, false);
+            for (int st = 0; st < kLseStages && st < issued; ++st) {
+                const int last_use = (issued - 1 - st) / kLseStages;
+                tc::mbar_wait(bar(kLseBarBFull + st), last_use & 1, abort_flag, kLseWaitLimit, false);
+            }
+            tc::mbar_wait(bar(kLseBarAFull), 0, abort_flag, kLseWaitLimit, false);
         }
         __syncwarp();
     } else {
@@ -478,12 +554,15 @@ __global__ __launch_bounds__(kLseThreads, 2) void lse_kernel(const __grid_consta
         const int64_t global_row = head * args.head_rows + row;
         half* out = args.lse + global_row * args.ld;
         const uint32_t lane_base = tmem + (static_cast<uint32_t>(warp * 32) << 16);
-        float mx[4] = {-FLT_MAX, -FLT_MAX, -FLT_MAX, -FLT_MAX};
-        float dn[4] = {0.f, 0.f, 0.f, 0.f};
+        uint64_t mx[2] = {pack2(-FLT_MAX, -FLT_MAX), pack2(-FLT_MAX, -FLT_MAX)};
+        uint64_t dn[2] = {0, 0};
+        const bool tma_out = args.vector_rows;
+        const int swz = (lane >> 1) & 3;
         bool ok = true;
         for (int t = 0; t < tiles; ++t) {
             const int b = t & 1;
-            if (!tc::mbar_wait_warp(bar(kLseBarTFull + b), (t >> 1) & 1, abort_flag, kLseWaitLimit)) {
+            if (!tc::mbar_wait_warp(bar(kLseBarTFull + b), (t >> 1) & 1, abort_flag, kLseWaitLimit,
+                                    tc::kLongWaitHintNs)) {
                 ok = false;
                 break;
             }
@@ -497,20 +576,47 @@ __global__ __launch_bounds__(kLseThreads, 2) void lse_kernel(const __grid_consta
             tc::fence_before_sync();
             tc::mbar_arrive(bar(kLseBarTEmpty + b));
             const int j0 = t * kLseTileBlocks;
-            if (j0 + kLseTileBlocks <= args.fine_blocks) {
-                lse_tile<true>(lo, j0, args.fine_blocks, out, valid, args.vector_rows, mx, dn);
-                lse_tile<true>(hi, j0 + 16, args.fine_blocks, out, valid, args.vector_rows, mx, dn);
+            const bool full = j0 + kLseTileBlocks <= args.fine_blocks;
+            if (tma_out) {
+                // Staging buffer b of this warp: the store issued from it two tiles
+                // ago must have finished reading it.
+                const uint32_t buf = base + kLseOffOut + (warp * 2 + b) * kLseOutBufBytes;
+                if (lane == 0) tc::bulk_wait_read<1>();
+                __syncwarp();
+                const uint32_t row_addr = buf + lane * kLseStageRowBytes;
+                if (full) {
+                    lse_tile<true, true>(lo, j0, args.fine_blocks, out, valid, row_addr, 0, swz, mx, dn);
+                    lse_tile<true, true>(hi, j0 + 16, args.fine_blocks, out, valid, row_addr, 2, swz, mx, dn);
+                } else {
+                    lse_tile<false, true>(lo, j0, args.fine_blocks, out, valid, row_addr, 0, swz, mx, dn);
+                    lse_tile<false, true>(hi, j0 + 16, args.fine_blocks, out, valid, row_addr, 2, swz, mx, dn);
+                }
+                tc::fence_proxy_async_smem();
+                __syncwarp();
+                if (lane == 0) {
+                    tc::tma_store_3d(&maps.out, buf, j0, static_cast<int32_t>(row0 + warp * 32),
+                                     static_cast<int32_t>(head));
+                    tc::bulk_commit();
+                }
+            } else if (full) {
+                lse_tile<true, false>(lo, j0, args.fine_blocks, out, valid, 0, 0, 0, mx, dn);
+                lse_tile<true, false>(hi, j0 + 16, args.fine_blocks, out, valid, 0, 0, 0, mx, dn);
             } else {
-                lse_tile<false>(lo, j0, args.fine_blocks, out, valid, args.vector_rows, mx, dn);
-                lse_tile<false>(hi, j0 + 16, args.fine_blocks, out, valid, args.vector_rows, mx, dn);
+                lse_tile<false, false>(lo, j0, args.fine_blocks, out, valid, 0, 0, 0, mx, dn);
+                lse_tile<false, false>(hi, j0 + 16, args.fine_blocks, out, valid, 0, 0, 0, mx, dn);
             }
         }
+        // Every store issued above has completed before the CTA may exit.
+        if (tma_out && lane == 0) tc::bulk_wait<0>();
+        __syncwarp();
         if (ok && valid) {
             // (c0 + c1) + (c2 + c3), each merge in the reference's operand order.
-            float m01 = mx[0], d01 = dn[0];
-            combine_lse(m01, d01, mx[1], dn[1]);
-            float m23 = mx[2], d23 = dn[2];
-            combine_lse(m23, d23, mx[3], dn[3]);
+            const float2 m0 = unpack2(mx[0]), m1 = unpack2(mx[1]);
+            const float2 d0 = unpack2(dn[0]), d1 = unpack2(dn[1]);
+            float m01 = m0.x, d01 = d0.x;
+            combine_lse(m01, d01, m0.y, d0.y);
+            float m23 = m1.x, d23 = d1.x;
+            combine_lse(m23, d23, m1.y, d1.y);
             combine_lse(m01, d01, m23, d23);
             args.lse_max[global_row] = m01;
             args.lse_den[global_row] = d01;
@@ -519,7 +625,7 @@ __global__ __launch_bounds__(kLseThreads, 2) void lse_kernel(const __grid_consta
 
     tc::fence_before_sync();
     __syncthreads();
-    if (warp == kLseLoadWarp) {
+    if (warp == kLseCtlWarp) {
         tc::fence_after_sync();
         tc::tmem_dealloc(tmem, kLseTmemColumns);
     }
@@ -624,6 +730,10 @@ cudaError_t launch_lse(const bf16* scaled, const bf16* pooled, int64_t bh, int64
     const int64_t head_rows = qb * kCentroids;
     if ((err = encode_rows(&maps.centroids, scaled, bh * head_rows, kLseRows)) != cudaSuccess) return err;
     if ((err = encode_rows(&maps.keys, pooled, bh * fine_blocks * kReps, kLseTileKeys)) != cudaSuccess) return err;
+    const bool vector_rows = ld % 8 == 0 && (reinterpret_cast<uintptr_t>(lse) & 15) == 0;
+    if (vector_rows &&
+        (err = encode_half_rows3d(&maps.out, lse, fine_blocks, head_rows, bh, ld, kLseTileBlocks, 32)) != cudaSuccess)
+        return err;
     LseArgs args{};
     args.head_rows = head_rows;
     args.ld = ld;
@@ -633,7 +743,7 @@ cudaError_t launch_lse(const bf16* scaled, const bf16* pooled, int64_t bh, int64
     args.lse_max = lse_max;
     args.lse_den = lse_den;
     args.error = device_error_word();
-    args.vector_rows = ld % 8 == 0 && (reinterpret_cast<uintptr_t>(lse) & 15) == 0;
+    args.vector_rows = vector_rows;
     err = cudaFuncSetAttribute(lse_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                static_cast<int>(kLseSmemBytes));
     if (err != cudaSuccess) return err;

@@ -10,7 +10,10 @@ namespace tc {
 
 // ---- mbarriers ------------------------------------------------------------------
 
-constexpr uint32_t kSuspendHintNs = 0;  // no suspend hint: measured no gain from sleeping waiters
+constexpr uint32_t kSuspendHintNs = 0;  // default: poll (the prefill's waits are short)
+// For waiters that expect to wait long (a control thread waiting on a slower
+// epilogue): sleep until the phase completes, at most this long per poll.
+constexpr uint32_t kLongWaitHintNs = 100000;
 
 __device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
     asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;\n" ::"r"(bar), "r"(count));
@@ -50,11 +53,12 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity, uin
 // whichever comes first, or, when `honor_abort`, as soon as another thread of
 // the CTA raised *abort.
 __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatile int* abort,
-                                          uint64_t limit_cycles, bool honor_abort = true) {
-    if (mbar_try_wait(bar, parity)) return true;
+                                          uint64_t limit_cycles, bool honor_abort = true,
+                                          uint32_t suspend_ns = kSuspendHintNs) {
+    if (mbar_try_wait(bar, parity, suspend_ns)) return true;
     const long long start = clock64();
     for (uint32_t spin = 1; spin < (1u << 28); ++spin) {
-        if (mbar_try_wait(bar, parity)) return true;
+        if (mbar_try_wait(bar, parity, suspend_ns)) return true;
         if ((spin & 63) == 0) {
             if (honor_abort && *abort) return false;
             if (static_cast<uint64_t>(clock64() - start) > limit_cycles) break;
@@ -67,8 +71,8 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatil
 // mbar_wait for all 32 lanes of a warp with a warp-uniform outcome, so that a
 // warp never splits before a .sync.aligned tcgen05 instruction.
 __device__ __forceinline__ bool mbar_wait_warp(uint32_t bar, uint32_t parity, volatile int* abort,
-                                               uint64_t limit_cycles) {
-    const bool ok = mbar_wait(bar, parity, abort, limit_cycles);
+                                               uint64_t limit_cycles, uint32_t suspend_ns = kSuspendHintNs) {
+    const bool ok = mbar_wait(bar, parity, abort, limit_cycles, true, suspend_ns);
     return __all_sync(0xffffffffu, ok);
 }
 
@@ -244,6 +248,26 @@ __device__ __forceinline__ void tma_load_2d(uint32_t dst, const void* tmap, int3
 // ---- cp.async with zero fill -------------------------------------------------------------
 
 // Copies 16 bytes, or writes 16 zero bytes when `valid` is false (no global read).
+// Store a box from shared memory through a 3-D tensor map (bulk async group);
+// elements outside the tensor are not written.
+__device__ __forceinline__ void tma_store_3d(const void* tmap, uint32_t src, int32_t x, int32_t y, int32_t z) {
+    asm volatile(
+        "cp.async.bulk.tensor.3d.global.shared::cta.bulk_group [%0, {%2, %3, %4}], [%1];\n" ::"l"(tmap),
+        "r"(src), "r"(x), "r"(y), "r"(z)
+        : "memory");
+}
+__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;\n" ::: "memory"); }
+// Wait until at most N committed bulk groups of this thread still read shared memory.
+template <int N>
+__device__ __forceinline__ void bulk_wait_read() {
+    asm volatile("cp.async.bulk.wait_group.read %0;\n" ::"n"(N) : "memory");
+}
+// Wait until at most N committed bulk groups of this thread are incomplete.
+template <int N>
+__device__ __forceinline__ void bulk_wait() {
+    asm volatile("cp.async.bulk.wait_group %0;\n" ::"n"(N) : "memory");
+}
+
 __device__ __forceinline__ void cp_async_16_zfill(uint32_t dst, const void* src, bool valid) {
     const uint32_t bytes = valid ? 16u : 0u;
     asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;\n" ::"r"(dst), "l"(src), "r"(bytes) : "memory");

@@ -39,4 +39,22 @@ inline cudaError_t encode_rows(CUtensorMap* map, const void* base, int64_t rows,
     return r == CUDA_SUCCESS ? cudaSuccess : cudaErrorInvalidValue;
 }
 
+// fp16 [heads][rows][ld] (row stride ld elements, ld % 8 == 0) for box stores of
+// box_x elements x box_y rows of one head, 64-byte swizzle; the tensor is
+// `cols` wide, so columns past it and rows past `rows` are never written.
+inline cudaError_t encode_half_rows3d(CUtensorMap* map, void* base, int64_t cols, int64_t rows, int64_t heads,
+                                      int64_t ld, uint32_t box_x, uint32_t box_y) {
+    auto encode = tensor_map_encoder();
+    if (encode == nullptr) return cudaErrorNotSupported;
+    const cuuint64_t dims[3] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(rows),
+                                static_cast<cuuint64_t>(heads)};
+    const cuuint64_t strides[2] = {static_cast<cuuint64_t>(ld) * 2, static_cast<cuuint64_t>(ld * rows) * 2};
+    const cuuint32_t box[3] = {box_x, box_y, 1};
+    const cuuint32_t elem_strides[3] = {1, 1, 1};
+    const CUresult r = encode(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, base, dims, strides, box, elem_strides,
+                              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_64B,
+                              CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS ? cudaSuccess : cudaErrorInvalidValue;
+}
+
 }  // namespace abx
