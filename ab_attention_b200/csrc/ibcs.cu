@@ -17,6 +17,7 @@
 // This file must be compiled with --use_fast_math (as csrc/ibcs.cu is).
 #include "common.cuh"
 #include "ibcs.cuh"
+#include "f32x2.cuh"
 #include "tcgen05.cuh"
 #include "tma_host.cuh"
 
@@ -331,35 +332,6 @@ __device__ __forceinline__ void combine_lse(float& maximum, float& denominator, 
     maximum = next;
 }
 
-// ---- packed f32x2 arithmetic (sm_100): two independent IEEE operations per
-// instruction, flushing subnormals like the --use_fast_math scalar forms ----
-__device__ __forceinline__ uint64_t pack2(float x, float y) {
-    uint64_t r;
-    asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(x), "f"(y));
-    return r;
-}
-__device__ __forceinline__ float2 unpack2(uint64_t v) {
-    float2 r;
-    asm("mov.b64 {%0, %1}, %2;" : "=f"(r.x), "=f"(r.y) : "l"(v));
-    return r;
-}
-__device__ __forceinline__ uint64_t add2(uint64_t a, uint64_t b) {
-    uint64_t d;
-    asm("add.rn.ftz.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
-    return d;
-}
-__device__ __forceinline__ uint64_t sub2(uint64_t a, uint64_t b) {
-    uint64_t d;
-    asm("sub.rn.ftz.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
-    return d;
-}
-__device__ __forceinline__ uint64_t fma2(uint64_t a, uint64_t b, uint64_t c) {
-    uint64_t d;
-    asm("fma.rn.ftz.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
-    return d;
-}
-constexpr uint64_t kOnes2 = 0x3F8000003F800000ull;  // (1.0f, 1.0f)
-constexpr uint64_t kZeros2 = 0;
 
 // The reference's pair_lse (csrc/ibcs.cu:339-343) for two blocks A and B, from
 // their raw representative scores with its "+ 1" (log2 of the representative

@@ -35,6 +35,7 @@
 #include <cudaTypedefs.h>
 
 #include "common.cuh"
+#include "f32x2.cuh"
 #include "ibcs.cuh"
 #include "tcgen05.cuh"
 #include "tma_host.cuh"
@@ -340,6 +341,8 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const PrefillArgs 
             const uint32_t s_col = lane_base + col_s(g);
             // Pass 1: row max of x = s * kappa + w over the tile, streaming S out of
             // TMEM 16 columns at a time (double-buffered), 4 independent chains.
+            // x is monotone in s within a granule (one w, kappa > 0), so the max
+            // of a granule is fma(max s, kappa, w): one FFMA per four columns.
             float part_max[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
             {
                 uint32_t buf[2][kChunk];
@@ -352,10 +355,10 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const PrefillArgs 
 #pragma unroll
                     for (int q4 = 0; q4 < kChunk / 4; ++q4) {
                         const float w = __shfl_sync(0xffffffffu, w_lane, c * (kChunk / 4) + q4);
-#pragma unroll
-                        for (int e = 0; e < 4; ++e)
-                            part_max[q4] =
-                                fmaxf(part_max[q4], fmaf(__uint_as_float(buf[c & 1][4 * q4 + e]), args.kappa, w));
+                        const uint32_t* g4 = buf[c & 1] + 4 * q4;
+                        const float smax = fmaxf(fmaxf(__uint_as_float(g4[0]), __uint_as_float(g4[1])),
+                                                 fmaxf(__uint_as_float(g4[2]), __uint_as_float(g4[3])));
+                        part_max[q4] = fmaxf(part_max[q4], fmaf(smax, args.kappa, w));
                     }
                     if (c + 1 < kTileKeys / kChunk) {
                         tc::tmem_wait_ld();
@@ -390,8 +393,10 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const PrefillArgs 
             }
             // Pass 2: P = 2^(s * kappa + (w - m)) as bf16 pairs, re-reading S; chunk c's
             // 8 packed words overwrite S columns [8c, 8c + 8), which no later chunk reads.
-            float part_sum[4] = {0.f, 0.f, 0.f, 0.f};
+            // Column pairs go through packed f32x2 FMAs and sums.
+            uint64_t part_sum[2] = {kZeros2, kZeros2};
             {
+                const uint64_t kappa2 = pack2(args.kappa, args.kappa);
                 uint32_t buf[2][kChunk];
                 tc::tmem_ld16(s_col, buf[0]);
                 tc::tmem_wait_ld();
@@ -401,13 +406,20 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const PrefillArgs 
                     if (c + 1 < kTileKeys / kChunk) tc::tmem_ld16(s_col + kChunk * (c + 1), buf[(c + 1) & 1]);
                     uint32_t packed[kChunk / 2];
 #pragma unroll
-                    for (int e = 0; e < kChunk / 2; ++e) {
-                        const float wm = __shfl_sync(0xffffffffu, w_lane, c * (kChunk / 4) + (e >> 1)) - m_used;
-                        const float p0 = exp2f(fmaf(__uint_as_float(buf[c & 1][2 * e]), args.kappa, wm));
-                        const float p1 = exp2f(fmaf(__uint_as_float(buf[c & 1][2 * e + 1]), args.kappa, wm));
-                        part_sum[e & 3] += p0 + p1;
-                        __nv_bfloat162 pair = __floats2bfloat162_rn(p0, p1);
-                        packed[e] = *reinterpret_cast<uint32_t*>(&pair);
+                    for (int q4 = 0; q4 < kChunk / 4; ++q4) {
+                        const float wm = __shfl_sync(0xffffffffu, w_lane, c * (kChunk / 4) + q4) - m_used;
+                        const uint64_t wm2 = pack2(wm, wm);
+#pragma unroll
+                        for (int h = 0; h < 2; ++h) {
+                            const int e = 2 * q4 + h;
+                            const uint64_t s2 = (static_cast<uint64_t>(buf[c & 1][2 * e + 1]) << 32) | buf[c & 1][2 * e];
+                            const float2 x = unpack2(fma2(s2, kappa2, wm2));
+                            const float p0 = exp2f(x.x);
+                            const float p1 = exp2f(x.y);
+                            part_sum[h] = add2(part_sum[h], pack2(p0, p1));
+                            __nv_bfloat162 pair = __floats2bfloat162_rn(p0, p1);
+                            packed[e] = *reinterpret_cast<uint32_t*>(&pair);
+                        }
                     }
                     tc::tmem_st8(s_col + (kChunk / 2) * c, packed);
                     if (c + 1 < kTileKeys / kChunk) {
@@ -416,7 +428,9 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const PrefillArgs 
                     }
                 }
             }
-            l_sum += (part_sum[0] + part_sum[1]) + (part_sum[2] + part_sum[3]);
+            const float2 ps0 = unpack2(part_sum[0]);
+            const float2 ps1 = unpack2(part_sum[1]);
+            l_sum += (ps0.x + ps0.y) + (ps1.x + ps1.y);
             tc::tmem_wait_st();
             tc::fence_before_sync();
             tc::mbar_arrive(bar(kBarPFull + g));
