@@ -9,7 +9,7 @@
 // text). o = sum 2^(l-m) v / sum 2^(l-m) and lse = m + log2(sum): the HT ratio
 // estimator of softmax attention.
 //
-// One CTA per row, 128-key tiles, warp-specialised (16 warps):
+// One CTA per row, 128-key tiles, warp-specialised (20 warps):
 //   warps 0-3, 4-7  two softmax warpgroups; group g takes the tiles t with
 //              t % 2 == g, so two independent streams of dependent math share
 //              each SM sub-partition. Thread i of a group owns query row i =
@@ -21,7 +21,7 @@
 //   warp  8    TMEM allocation + MMA issue (one thread): S(t) = Q K(t)^T with
 //              both operands in shared memory, O(t%2) += P(t) V(t) with P read
 //              from TMEM.
-//   warps 9-11 gather Q and the K tiles, warps 12-15 the V tiles, with TMA: an
+//   warps 9-13 gather Q and the K tiles, warps 14-19 the V tiles, with TMA: an
 //              operand tile is 64 boxes of 4 rows x 64 columns (32 granules x
 //              two 64-dim slabs), one box per lane, landing 128-byte swizzled at
 //              the granule's rows of the UMMA operand tile; the stage mbarrier
@@ -29,6 +29,13 @@
 //              row (zero fill).
 // TMEM: S/P double buffer in columns [0,128) and [128,256), O of group 0 in
 // [256,384), O of group 1 in [384,512).
+// Stages: a V stage is free only once PV of its tile has run, which follows the
+// tile's softmax, while a K stage frees as soon as S has run; so V gets three
+// stages and K two.
+// Registers: the launch gives every thread kLaunchRegs; the softmax warpgroups
+// then raise theirs to kSoftmaxRegs and the MMA/gather warpgroups lower theirs
+// to kProducerRegs (setmaxnreg). The split fits the launch's allocation
+// (checked at compile time and against the kernel's attributes on the host).
 // Every mbarrier wait is bounded; on expiry the CTA drains its copies and MMAs,
 // frees TMEM, records ABX_ERR_DEVICE_TIMEOUT in the device error word and exits.
 #include <cuda.h>
@@ -48,8 +55,8 @@ namespace {
 
 constexpr int kTileKeys = 128;
 constexpr int kTileGranules = kTileKeys / kKv4;
-constexpr int kKStages = 3;
-constexpr int kVStages = 2;
+constexpr int kKStages = 2;
+constexpr int kVStages = 3;
 constexpr uint32_t kSlabBytes = 128 * 128;       // 128 rows x 64 bf16
 constexpr uint32_t kTileBytes = 2 * kSlabBytes;  // one 128 x 128 bf16 operand tile
 constexpr int kSoftmaxGroups = 2;
@@ -58,14 +65,21 @@ constexpr int kMmaWarp = 8;
 // 64-dim slabs, box b = granule b/2, slab b%2); gather warp p of P issues boxes
 // p, p+P, p+2P, ... one per lane. (A TMA request costs the issuing warp tens of
 // cycles per active lane, so the requests are spread over several warps.)
-constexpr int kKGatherWarps = 3;
-constexpr int kVGatherWarps = 4;
+constexpr int kKGatherWarps = 5;
+constexpr int kVGatherWarps = 6;
 constexpr int kBoxesPerTile = 2 * kTileGranules;
 constexpr uint32_t kBoxBytes = kKv4 * 128;
 constexpr int kKLoadWarp = kMmaWarp + 1;                // first K warp (also loads Q)
 constexpr int kVLoadWarp = kKLoadWarp + kKGatherWarps;  // first V warp
 constexpr int kThreads = (kVLoadWarp + kVGatherWarps) * 32;
 constexpr int kChunk = 16;                              // TMEM columns per softmax step
+constexpr int kLaunchRegs = 96;                         // 640 threads x 96 = 61,440 of 65,536
+constexpr int kSoftmaxRegs = 168;                       // warpgroups 0-1
+constexpr int kProducerRegs = 48;                       // warpgroups 2-4 (MMA + gather warps)
+static_assert(kThreads == 640, "register split below assumes 20 warps");
+static_assert(kThreads * kLaunchRegs <= 65536, "launch register allocation exceeds the SM");
+static_assert(8 * 32 * kSoftmaxRegs + (kThreads - 8 * 32) * kProducerRegs <= kThreads * kLaunchRegs,
+              "setmaxnreg split exceeds the launch allocation (the increase would never complete)");
 
 constexpr uint32_t kTmemColumns = 512;
 __device__ __forceinline__ constexpr uint32_t col_s(int b) { return 128u * static_cast<uint32_t>(b); }
@@ -214,6 +228,10 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const PrefillArgs 
     __syncthreads();
     tc::fence_after_sync();
     const uint32_t tmem = *tmem_slot;
+
+    // Register split by warpgroup (every warp of a warpgroup executes the same one).
+    if (warp < kMmaWarp) asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;\n" ::"n"(kSoftmaxRegs));
+    else asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;\n" ::"n"(kProducerRegs));
 
     if (warp >= kKLoadWarp) {
         // ---- producers: one TMA box per lane per operand tile --------------------------------
@@ -534,6 +552,13 @@ cudaError_t launch_prefill(const bf16* q, const bf16* k, const bf16* v, int64_t 
     err = cudaFuncSetAttribute(prefill_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                static_cast<int>(kSmemBytes));
     if (err != cudaSuccess) return err;
+    // The setmaxnreg increase only completes if the launch allocated at least the
+    // split's registers; refuse to launch otherwise.
+    cudaFuncAttributes attr{};
+    if ((err = cudaFuncGetAttributes(&attr, prefill_kernel)) != cudaSuccess) return err;
+    if (static_cast<int64_t>(attr.numRegs) * kThreads <
+        static_cast<int64_t>(8 * 32 * kSoftmaxRegs + (kThreads - 8 * 32) * kProducerRegs))
+        return cudaErrorInvalidConfiguration;
     prefill_kernel<<<static_cast<unsigned>(bh * args.qb), kThreads, kSmemBytes, stream>>>(args, maps);
     return cudaGetLastError();
 }
