@@ -229,7 +229,7 @@ __device__ __forceinline__ void tmem_reg_fence(uint32_t (&r)[32]) {
 }
 __device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;\n" ::: "memory"); }
 
-// ---- TMA (tensor copies, no multicast) --------------------------------------------------
+// ---- TMA (tensor copies into this CTA only) --------------------------------------------------
 
 // Register `bytes` of expected transaction volume on `bar` together with one arrival.
 __device__ __forceinline__ void mbar_arrive_expect_tx(uint32_t bar, uint32_t bytes) {

@@ -85,10 +85,17 @@ def smooth_field(batch_heads: int, frames: int, height: int, width: int, *, dim:
     return q, k, v
 
 
-def make_inputs(shape: VideoShape, device="cuda", bh_slice: slice | None = None):
+def make_inputs(shape: VideoShape, device="cuda", bh_slice: slice | list | None = None):
     """Q/K/V [B, H, N, 128] for a configuration (cube-permuted when shape.cube),
-    plus (text_k, text_v) [B, H, 256, 128] when the configuration has text."""
-    heads = range(shape.batch_heads) if bh_slice is None else range(shape.batch_heads)[bh_slice]
+    plus (text_k, text_v) [B, H, 256, 128] when the configuration has text.
+    `bh_slice` (a slice or a list of flattened heads) selects heads; the result
+    is then [1, len, N, 128]."""
+    if bh_slice is None:
+        heads = range(shape.batch_heads)
+    elif isinstance(bh_slice, slice):
+        heads = range(shape.batch_heads)[bh_slice]
+    else:
+        heads = list(bh_slice)
     q, k, v = smooth_field(shape.batch_heads, shape.frames, shape.height, shape.width, dim=shape.dim,
                            seed=shape.seed, sigma=shape.sigma, device=device, heads=heads)
     if shape.cube:

@@ -58,6 +58,10 @@ def build(reference: Path = DEFAULT_REFERENCE, force: bool = False) -> Path | No
         build_directory=str(OUT),
         verbose=False,
     )
+    # Keep only the shared object: ninja's bookkeeping lists every toolkit
+    # header the build touched and is not needed to load the module.
+    for leftover in (".ninja_deps", ".ninja_log", "build.ninja", *[p.name for p in OUT.glob("*.o")]):
+        (OUT / leftover).unlink(missing_ok=True)
     return built_library()
 
 

@@ -70,6 +70,48 @@ def _worker(rank, world, port, result_path, fail_rank):
             pass
 
 
+def _block_worker(rank, world, port, result_path, chunks):
+    """Block-interleaved heads, each block all-gathered asynchronously into place."""
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=timedelta(seconds=10))
+    try:
+        x, _ = _reference()
+        heads = shard.rank_heads(BH, world, rank, chunks)
+        offsets = shard.shard_offsets(shard.layer_offsets(BH, TOKENS, SEED, "cpu"), TOKENS, heads)
+        qb = math.ceil(TOKENS / 128)
+        ch = len(heads) // chunks
+        out = torch.empty_like(x)
+        works = []
+        for c in range(chunks):
+            block = torch.stack([_per_head(x[h], offsets[i * qb:(i + 1) * qb])
+                                 for i, h in enumerate(heads) if c * ch <= i < (c + 1) * ch])
+            works.append(shard.gather_block(out, block, world, c, async_op=True))
+        for w in works:
+            w.wait()
+        if rank == 0:
+            torch.save({"status": "ok", "full": out}, result_path)
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("world,chunks", [(2, 2), (4, 2), (2, 4)])
+def test_block_interleaved_gather_matches_single_process(tmp_path, world, chunks):
+    path = str(tmp_path / "out.pt")
+    mp.start_processes(_block_worker, args=(world, _free_port(), path, chunks), nprocs=world, join=True,
+                       start_method="spawn")
+    _, want = _reference()
+    assert torch.equal(torch.load(path)["full"], want)
+
+
+def test_rank_heads_partition_every_head_once():
+    for world, chunks in [(1, 1), (2, 4), (4, 2), (8, 1)]:
+        owned = sorted(h for r in range(world) for h in shard.rank_heads(BH, world, r, chunks))
+        assert owned == list(range(BH))
+    assert shard.chunk_count(80, 8) == 2 and shard.chunk_count(80, 2) == 4 and shard.chunk_count(24, 8) == 3
+    with pytest.raises(ValueError):
+        shard.rank_heads(BH, 3, 0)
+
+
 @pytest.mark.parametrize("world", [2, 4])
 def test_sharded_layer_matches_single_process(tmp_path, world):
     path = str(tmp_path / "out.pt")
