@@ -1,5 +1,8 @@
 """B200-native AB-Attention sparse-attention hot path (IBCS + SIP + HT-weighted sparse prefill)."""
-from .attention import SamplePlan, ab_attention, apply_plan, build_plan, dense_attention
+from .attention import (SamplePlan, ab_attention, apply_plan, build_plan, dense_attention,
+                        dense_cross_attention, paged_attention)
 from .layout import cube_layout
 
-__all__ = ["SamplePlan", "ab_attention", "apply_plan", "build_plan", "dense_attention", "cube_layout"]
+__all__ = ["SamplePlan", "ab_attention", "apply_plan", "build_plan", "dense_attention", "dense_cross_attention",
+           "paged_attention", "cube_layout", "VideoAttention", "hunyuan_attention"]
+from .video import VideoAttention, hunyuan_attention  # noqa: E402

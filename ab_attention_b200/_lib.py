@@ -35,6 +35,7 @@ _SIGNATURES = {
     "abx_build_plan_static": ([_p, _p, _i64, _i64, _p, _i64, _p, _p, _p], ctypes.c_int),
     "abx_sparse_prefill": ([_p, _p, _p, _i64, _i64, _p, _p, _i64, _p, _p, _i64, _p, _p, _p], ctypes.c_int),
     "abx_dense_prefill": ([_p, _p, _p, _i64, _i64, _p, _p, _p], ctypes.c_int),
+    "abx_cross_prefill": ([_p, _i64, _p, _p, _i64, _i64, _p, _p, _i64, _p, _p, _i64, _p, _p, _p], ctypes.c_int),
 }
 
 _lib = None

@@ -100,7 +100,7 @@ def paged_attention(q, k, v, descriptor, log_weights, *, return_lse=False, text_
 
     Same signature, checks and outputs as the reference's FlashInfer adapter;
     the work is one tcgen05 kernel launch. ``text_kv=(text_k, text_v)``
-    ([B,H,T,128] bf16, T % 4 == 0) appends T keys that every query block always
+    ([B,H,T,128] bf16, any T) appends T keys that every query block always
     includes with weight pi = 1. The optional base-2 LSE is [batch, heads, tokens]
     float32.
     """
@@ -117,8 +117,8 @@ def paged_attention(q, k, v, descriptor, log_weights, *, return_lse=False, text_
     if text_kv is not None:
         text_k, text_v = text_kv
         if (text_k.shape != text_v.shape or text_k.ndim != 4 or text_k.shape[:2] != q.shape[:2]
-                or text_k.shape[-1] != dim or text_k.shape[2] % 4):
-            raise ValueError("text_kv must be two [B,H,T,128] tensors with T divisible by 4")
+                or text_k.shape[-1] != dim or text_k.shape[2] == 0):
+            raise ValueError("text_kv must be two [B,H,T,128] tensors with T > 0")
         if text_k.dtype != q.dtype or text_v.dtype != q.dtype or text_k.device != q.device:
             raise ValueError("text_kv must be BF16 on the Q device")
         text_k = text_k.reshape(batch_heads, -1, dim).contiguous()
@@ -160,5 +160,36 @@ def dense_attention(q, k, v, *, return_lse=False):
     bh = batch * heads
     out, lse = ops.dense_prefill(q.reshape(bh, tokens, dim).contiguous(), k.reshape(bh, tokens, dim).contiguous(),
                                  v.reshape(bh, tokens, dim).contiguous(), return_lse=return_lse)
+    out = out.reshape_as(q)
+    return (out, lse.reshape(batch, heads, tokens)) if return_lse else out
+
+
+@torch.no_grad()
+def dense_cross_attention(q, k, v, *, extra_kv=None, return_lse=False):
+    """Softmax attention (scale 128^-0.5) of q [B,H,Nq,128] over every key of
+    k/v [B,H,Nk,128] (Nk % 4 == 0; k = v = None for none) followed by every key
+    of ``extra_kv=(k2, v2)`` [B,H,T,128] (any T). One launch of the prefill
+    kernel; used for the HunyuanVideo text and padding partitions."""
+    if q.ndim != 4 or q.dtype != torch.bfloat16 or q.shape[-1] != 128 or q.device.type != "cuda":
+        raise ValueError("q must be [B,H,N,128] bf16 on a CUDA device")
+    batch, heads, tokens, dim = q.shape
+    bh = batch * heads
+    def flat(x):
+        if x.shape[:2] != q.shape[:2] or x.shape[-1] != dim or x.dtype != q.dtype or x.device != q.device:
+            raise ValueError("keys must be [B,H,N,128] bf16 on the Q device")
+        return x.reshape(bh, x.shape[2], dim).contiguous()
+    k3 = v3 = None
+    if k is not None:
+        if k.shape != v.shape or k.shape[2] % 4:
+            raise ValueError("k and v must match with a token count divisible by 4")
+        k3, v3 = flat(k), flat(v)
+    tk = tv = None
+    if extra_kv is not None:
+        tk, tv = (flat(x) for x in extra_kv)
+        if tk.shape != tv.shape:
+            raise ValueError("extra keys and values must match")
+    samples = 0 if k3 is None else k3.shape[1] // 4
+    out, lse = ops.cross_prefill(q.reshape(bh, tokens, dim).contiguous(), k3, v3, samples=samples,
+                                 text_k=tk, text_v=tv, return_lse=return_lse)
     out = out.reshape_as(q)
     return (out, lse.reshape(batch, heads, tokens)) if return_lse else out

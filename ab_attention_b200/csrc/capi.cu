@@ -353,13 +353,12 @@ int abx_sparse_prefill(const void* q, const void* k, const void* v, int64_t bh, 
         return fail(ABX_ERR_INVALID_ARGUMENT, "samples must be in [0, seq/4] (got %lld)", (long long)samples);
     if (samples > 0 && (ids == nullptr || log_weights == nullptr))
         return fail(ABX_ERR_INVALID_ARGUMENT, "ids and log_weights must be non-null");
-    if (text_tokens < 0 || text_tokens % abx::kKv4 != 0)
-        return fail(ABX_ERR_INVALID_ARGUMENT, "text token count must be a non-negative multiple of 4");
+    if (text_tokens < 0) return fail(ABX_ERR_INVALID_ARGUMENT, "negative text token count");
     if (text_tokens > 0 && (!text_k || !text_v || !aligned16(text_k) || !aligned16(text_v)))
         return fail(ABX_ERR_INVALID_ARGUMENT, "text_k/text_v must be non-null and 16-byte aligned");
-    if (samples + text_tokens / abx::kKv4 <= 0)
+    if (samples + (text_tokens + abx::kKv4 - 1) / abx::kKv4 <= 0)
         return fail(ABX_ERR_INVALID_ARGUMENT, "every row needs at least one key block");
-    return check_cuda(abx::launch_prefill(static_cast<const abx::bf16*>(q), static_cast<const abx::bf16*>(k),
+    return check_cuda(abx::launch_prefill(static_cast<const abx::bf16*>(q), seq, static_cast<const abx::bf16*>(k),
                                           static_cast<const abx::bf16*>(v), bh, seq, ids, log_weights, samples,
                                           static_cast<const abx::bf16*>(text_k),
                                           static_cast<const abx::bf16*>(text_v), text_tokens,
@@ -373,10 +372,40 @@ int abx_dense_prefill(const void* q, const void* k, const void* v, int64_t bh, i
     if (!q || !k || !v || !o) return fail(ABX_ERR_INVALID_ARGUMENT, "q, k, v and o must be non-null");
     if (!aligned16(q) || !aligned16(k) || !aligned16(v) || !aligned16(o))
         return fail(ABX_ERR_INVALID_ARGUMENT, "q, k, v and o must be 16-byte aligned");
-    return check_cuda(abx::launch_prefill(static_cast<const abx::bf16*>(q), static_cast<const abx::bf16*>(k),
+    return check_cuda(abx::launch_prefill(static_cast<const abx::bf16*>(q), seq, static_cast<const abx::bf16*>(k),
                                           static_cast<const abx::bf16*>(v), bh, seq, nullptr, nullptr,
                                           seq / abx::kKv4, nullptr, nullptr, 0, static_cast<abx::bf16*>(o), lse,
                                           stream),
+                      "prefill launch");
+}
+
+int abx_cross_prefill(const void* q, int64_t q_tokens, const void* k, const void* v, int64_t kv_tokens, int64_t bh,
+                      const int32_t* ids, const float* log_weights, int64_t samples, const void* text_k,
+                      const void* text_v, int64_t text_tokens, void* o, float* lse, abx_stream_t stream) {
+    if (bh <= 0 || q_tokens <= 0) return fail(ABX_ERR_INVALID_ARGUMENT, "bad query shape");
+    if (kv_tokens < 0 || kv_tokens % abx::kKv4 != 0)
+        return fail(ABX_ERR_INVALID_ARGUMENT, "key token count must be a non-negative multiple of 4");
+    if (kv_tokens / abx::kKv4 > abx::kMaxFineBlocks)
+        return fail(ABX_ERR_UNSUPPORTED, "more than %d key blocks", abx::kMaxFineBlocks);
+    if (!q || !o || !aligned16(q) || !aligned16(o))
+        return fail(ABX_ERR_INVALID_ARGUMENT, "q and o must be non-null and 16-byte aligned");
+    if (samples < 0 || samples > kv_tokens / abx::kKv4)
+        return fail(ABX_ERR_INVALID_ARGUMENT, "samples must be in [0, kv_tokens/4] (got %lld)", (long long)samples);
+    if (samples > 0 && (!k || !v || !aligned16(k) || !aligned16(v)))
+        return fail(ABX_ERR_INVALID_ARGUMENT, "k and v must be non-null and 16-byte aligned");
+    if ((ids == nullptr) != (log_weights == nullptr))
+        return fail(ABX_ERR_INVALID_ARGUMENT, "ids and log_weights are given together (or neither: dense)");
+    if (text_tokens < 0) return fail(ABX_ERR_INVALID_ARGUMENT, "negative text token count");
+    if (text_tokens > 0 && (!text_k || !text_v || !aligned16(text_k) || !aligned16(text_v)))
+        return fail(ABX_ERR_INVALID_ARGUMENT, "text_k/text_v must be non-null and 16-byte aligned");
+    if (samples + (text_tokens + abx::kKv4 - 1) / abx::kKv4 <= 0)
+        return fail(ABX_ERR_INVALID_ARGUMENT, "every row needs at least one key");
+    return check_cuda(abx::launch_prefill(static_cast<const abx::bf16*>(q), q_tokens,
+                                          static_cast<const abx::bf16*>(k), static_cast<const abx::bf16*>(v), bh,
+                                          kv_tokens, ids, log_weights, samples,
+                                          static_cast<const abx::bf16*>(text_k),
+                                          static_cast<const abx::bf16*>(text_v), text_tokens,
+                                          static_cast<abx::bf16*>(o), lse, stream),
                       "prefill launch");
 }
 

@@ -24,7 +24,7 @@ cudaError_t launch_sip(const float* scores, const float* offsets, int64_t rows, 
                        int32_t* ids, float* log_weights, int64_t samples, cudaStream_t stream);
 
 // Sparse / dense prefill.
-cudaError_t launch_prefill(const bf16* q, const bf16* k, const bf16* v, int64_t bh, int64_t seq,
+cudaError_t launch_prefill(const bf16* q, int64_t q_tokens, const bf16* k, const bf16* v, int64_t bh, int64_t seq,
                            const int32_t* ids, const float* log_weights, int64_t samples,
                            const bf16* text_k, const bf16* text_v, int64_t text_tokens, bf16* o,
                            float* lse, cudaStream_t stream);

@@ -125,11 +125,13 @@ struct PrefillArgs {
     const bf16* text_v;
     bf16* o;
     float* lse;
-    int64_t seq;
-    int64_t qb;
+    int64_t seq;          // key tokens per head (k, v)
+    int64_t seq_q;        // query tokens per head (q, o, lse)
+    int64_t qb;           // ceil(seq_q / 128)
     int64_t text_tokens;
     int samples;
-    int granules;         // samples + text_tokens / 4
+    int granules;         // samples + ceil(text_tokens / 4)
+    int text_tail;        // text_tokens % 4: keys of the last text granule past it are masked
     int fine_blocks;      // seq / 4: valid ids are [0, fine_blocks)
     int64_t kv_rows;      // bh * seq: rows of the K/V tensor maps (an index >= this reads zeros)
     int64_t text_rows;    // bh * text_tokens
@@ -169,6 +171,27 @@ __device__ __forceinline__ int64_t granule_row(const PrefillArgs& a, int64_t hea
     return head * a.text_tokens + static_cast<int64_t>(slot - a.samples) * kKv4;
 }
 
+// In chunk c of the tile holding the last slot, scores of that granule's keys
+// past the last text token (its first `tail` keys are valid) -> -inf; the
+// chunk's later columns belong to padding slots and are -inf already by weight.
+// Before the softmax of the tile holding the last slot: the scores of that
+// granule's keys past the last text token (its first `tail` keys are valid) are
+// set to -inf in TMEM, so both softmax passes exclude them. Warp-collective.
+__device__ __forceinline__ void mask_tail(uint32_t s_col, int last_slot, int tail) {
+    const int local = last_slot % kTileGranules;
+    const uint32_t col = s_col + kChunk * (local / (kChunk / kKv4));
+    const int first = (local % (kChunk / kKv4)) * kKv4 + tail;
+    uint32_t chunk[kChunk];
+    tc::tmem_ld16(col, chunk);
+    tc::tmem_wait_ld();
+    tc::tmem_reg_fence(chunk);
+#pragma unroll
+    for (int e = 0; e < kChunk; ++e)
+        if (e >= first) chunk[e] = 0xff800000u;
+    tc::tmem_st16(col, chunk);
+    tc::tmem_wait_st();
+}
+
 // Logit shift of granule `slot`: its SIP weight, 0 for text, -inf past the end.
 __device__ __forceinline__ float slot_weight(const PrefillArgs& a, const float* row_w, int slot) {
     if (slot >= a.granules) return -INFINITY;
@@ -193,7 +216,7 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const PrefillArgs 
     const int64_t row = blockIdx.x;
     const int64_t head = row / args.qb;
     const int64_t token0 = (row - head * args.qb) * kQueryBlock;
-    const int n = static_cast<int>(min(static_cast<int64_t>(kQueryBlock), args.seq - token0));
+    const int n = static_cast<int>(min(static_cast<int64_t>(kQueryBlock), args.seq_q - token0));
     const int tiles = (args.granules + kTileGranules - 1) / kTileGranules;
     const int32_t* row_ids = args.ids ? args.ids + row * args.samples : nullptr;
     const float* row_w = args.logw ? args.logw + row * args.samples : nullptr;
@@ -246,7 +269,7 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const PrefillArgs 
         if (warp == kKLoadWarp && lane == 0) {
             // Q tile: two 128-row x 64-column boxes (rows past the block are never stored).
             tc::mbar_arrive_expect_tx(bar(kBarQFull), kTileBytes);
-            const int32_t qy = static_cast<int32_t>(head * args.seq + token0);
+            const int32_t qy = static_cast<int32_t>(head * args.seq_q + token0);
             tc::tma_load_2d(base + kOffQ, &maps.q, 0, qy, bar(kBarQFull));
             tc::tma_load_2d(base + kOffQ + kSlabBytes, &maps.q, 64, qy, bar(kBarQFull));
         }
@@ -344,6 +367,9 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const PrefillArgs 
         float m_used = -INFINITY;
         float l_sum = 0.f;
         bool ok = true;
+        // The last text granule (the last slot) may hold fewer than 4 keys; in
+        // its tile the chunk holding it masks its columns past the last key.
+        const int tail_tile = args.text_tail ? (args.granules - 1) / kTileGranules : -1;
         // Lane j holds the weight of granule j of the current tile; the group's
         // next tile (t + 2) is read one step ahead.
         float w_next = slot_weight(args, row_w, g * kTileGranules + lane);
@@ -357,6 +383,7 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const PrefillArgs 
             }
             tc::fence_after_sync();
             const uint32_t s_col = lane_base + col_s(g);
+            if (t == tail_tile) mask_tail(s_col, args.granules - 1, args.text_tail);
             // Pass 1: row max of x = s * kappa + w over the tile, streaming S out of
             // TMEM 16 columns at a time (double-buffered), 4 independent chains.
             // x is monotone in s within a granule (one w, kappa > 0), so the max
@@ -473,7 +500,7 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const PrefillArgs 
             const float a0 = s0 * inv;
             const float a1 = s1 * inv;
             const uint32_t o1_col = lane_base + col_o(1);
-            bf16* out_row = args.o + (head * args.seq + token0 + r) * kHeadDim;
+            bf16* out_row = args.o + (head * args.seq_q + token0 + r) * kHeadDim;
 #pragma unroll 1
             for (int c = 0; c < 128 / kChunk; ++c) {
                 uint32_t o0[kChunk], o1[kChunk];
@@ -500,7 +527,7 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const PrefillArgs 
                     reinterpret_cast<uint4*>(out_row + kChunk * c)[1] = packed[1];
                 }
             }
-            if (args.lse != nullptr && r < n) args.lse[head * args.seq + token0 + r] = m + log2f(l);
+            if (args.lse != nullptr && r < n) args.lse[head * args.seq_q + token0 + r] = m + log2f(l);
         }
     }
 
@@ -516,7 +543,9 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const PrefillArgs 
 
 }  // namespace
 
-cudaError_t launch_prefill(const bf16* q, const bf16* k, const bf16* v, int64_t bh, int64_t seq,
+static int64_t rows_or(int64_t rows, int64_t fallback) { return rows > 0 ? rows : fallback; }
+
+cudaError_t launch_prefill(const bf16* q, int64_t q_tokens, const bf16* k, const bf16* v, int64_t bh, int64_t seq,
                            const int32_t* ids, const float* log_weights, int64_t samples,
                            const bf16* text_k, const bf16* text_v, int64_t text_tokens, bf16* o,
                            float* lse, cudaStream_t stream) {
@@ -531,21 +560,25 @@ cudaError_t launch_prefill(const bf16* q, const bf16* k, const bf16* v, int64_t 
     args.o = o;
     args.lse = lse;
     args.seq = seq;
-    args.qb = ceil_div(seq, kQueryBlock);
+    args.seq_q = q_tokens;
+    args.qb = ceil_div(q_tokens, kQueryBlock);
     args.text_tokens = text_tokens;
+    args.text_tail = static_cast<int>(text_tokens % kKv4);
     args.samples = static_cast<int>(samples);
-    args.granules = static_cast<int>(samples + text_tokens / kKv4);
+    args.granules = static_cast<int>(samples + ceil_div(text_tokens, kKv4));
     args.fine_blocks = static_cast<int>(seq / kKv4);
-    args.kv_rows = bh * seq;
     args.text_rows = bh * text_tokens;
     args.kappa = qk_scale_log2();
     args.error = device_error_word();
     PrefillMaps maps;
     cudaError_t err;
-    if ((err = encode_rows(&maps.q, q, bh * seq, 128)) != cudaSuccess) return err;
+    if ((err = encode_rows(&maps.q, q, bh * q_tokens, 128)) != cudaSuccess) return err;
     const bool has_text = text_tokens > 0 && text_k != nullptr && text_v != nullptr;
     const void* sources[2][2] = {{k, has_text ? text_k : k}, {v, has_text ? text_v : v}};
-    const int64_t rows[2] = {bh * seq, has_text ? bh * text_tokens : bh * seq};
+    const bool has_video = seq > 0;
+    if (!has_video) sources[0][0] = sources[1][0] = has_text ? text_k : q;  // never read: no video slots
+    const int64_t rows[2] = {has_video ? bh * seq : bh, has_text ? bh * text_tokens : rows_or(bh * seq, bh)};
+    args.kv_rows = rows[0];  // first row past the video map: padding slots read zeros there
     for (int op = 0; op < 2; ++op)
         for (int src = 0; src < 2; ++src)
             if ((err = encode_rows(&maps.kv[op][src], sources[op][src], rows[src], kKv4)) != cudaSuccess) return err;

@@ -186,6 +186,23 @@ def dense_prefill(q3, k3, v3, *, return_lse=False):
     return o, lse_
 
 
+def cross_prefill(q3, k3, v3, *, ids=None, logw=None, samples=0, text_k=None, text_v=None, return_lse=False):
+    """q3 [BH,Nq,128] over `samples` granules of k3/v3 [BH,Nk,128] (the plan's ids
+    with their log weights, or the first `samples` in order when ids is None)
+    followed by every key of text_k/text_v [BH,T,128] (any T)."""
+    bh, q_tokens, _ = q3.shape
+    kv_tokens = 0 if k3 is None else k3.shape[1]
+    o = torch.empty_like(q3)
+    lse_ = torch.empty((bh, q_tokens), dtype=torch.float32, device=q3.device) if return_lse else None
+    text_tokens = 0 if text_k is None else text_k.shape[1]
+    lib = _lib.load()
+    with torch.cuda.device(q3.device):
+        _lib.check(lib.abx_cross_prefill(_lib.ptr(q3), q_tokens, _lib.ptr(k3), _lib.ptr(v3), kv_tokens, bh,
+                                         _lib.ptr(ids), _lib.ptr(logw), samples, _lib.ptr(text_k), _lib.ptr(text_v),
+                                         text_tokens, _lib.ptr(o), _lib.ptr(lse_), _lib.stream_of(q3)),
+                   "abx_cross_prefill")
+    return o, lse_
+
 # ---- torch.library registration ------------------------------------------------------
 # `torch.ops.ab_attention.{ibcs,sip,sparse_prefill}`: the custom-op form of the
 # same entry points, with a CUDA kernel only. A CPU tensor finds no kernel and

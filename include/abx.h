@@ -140,6 +140,20 @@ int abx_sparse_prefill(const void* q, const void* k, const void* v, int64_t bh, 
 int abx_dense_prefill(const void* q, const void* k, const void* v, int64_t bh, int64_t seq,
                       void* o, float* lse, abx_stream_t stream);
 
+/* Queries attending to keys of another length: q [bh, q_tokens, 128] against
+ * the KV4 granules named by ids ([bh * ceil(q_tokens/128), samples]; NULL ids
+ * and log_weights = the first `samples` granules of k/v in order, weight 0)
+ * of k, v [bh, kv_tokens, 128], followed by the text keys text_k, text_v
+ * [bh, text_tokens, 128] (any count; keys past text_tokens in the last
+ * granule are masked). o [bh, q_tokens, 128], lse [bh, q_tokens] (base 2) or
+ * NULL. No counterpart entry point in the reference: it covers the
+ * HunyuanVideo partitions its video.py:129-151 runs through FlashInfer (text
+ * queries over all video + text keys, and the padding partition with
+ * samples = 0 and the padding tokens as text keys). */
+int abx_cross_prefill(const void* q, int64_t q_tokens, const void* k, const void* v, int64_t kv_tokens, int64_t bh,
+                      const int32_t* ids, const float* log_weights, int64_t samples, const void* text_k,
+                      const void* text_v, int64_t text_tokens, void* o, float* lse, abx_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -90,3 +90,15 @@ def test_python_api_refuses_cpu_tensors():
     plan = (torch.zeros(8, 2, 32, dtype=torch.int32), torch.zeros(8, 2, 32))
     with pytest.raises(ValueError):
         apply_plan(q, q, q, plan)
+
+
+def test_cross_prefill_validates_before_launch():
+    lib = _lib.load()
+    p = ctypes.c_void_p(16)
+    # key token count must be a multiple of 4; samples within the keys; ids and weights together
+    assert lib.abx_cross_prefill(p, 10, p, p, 6, 1, None, None, 1, None, None, 0, p, None, None) == 1
+    assert lib.abx_cross_prefill(p, 10, p, p, 8, 1, None, None, 3, None, None, 0, p, None, None) == 1
+    assert lib.abx_cross_prefill(p, 10, p, p, 8, 1, p, None, 2, None, None, 0, p, None, None) == 1
+    # no keys at all; negative text count
+    assert lib.abx_cross_prefill(p, 10, None, None, 0, 1, None, None, 0, None, None, 0, p, None, None) == 1
+    assert lib.abx_cross_prefill(p, 10, p, p, 8, 1, None, None, 2, p, p, -1, p, None, None) == 1
