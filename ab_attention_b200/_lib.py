@@ -23,6 +23,7 @@ _SIGNATURES = {
     "abx_status_string": ([ctypes.c_int], ctypes.c_char_p),
     "abx_last_error": ([], ctypes.c_char_p),
     "abx_device_status": ([_p, ctypes.c_int, _p], ctypes.c_int),
+    "abx_selftest_wait_timeout": ([_i64, _p], ctypes.c_int),
     "abx_ibcs_cluster": ([_p, _i64, _i64, _p, _p, _p, _p, _p], ctypes.c_int),
     "abx_ibcs_pool": ([_p, _i64, _i64, _p, _p], ctypes.c_int),
     "abx_ibcs_lse": ([_p, _p, _i64, _i64, _i64, _p, _p, _p, _p], ctypes.c_int),

@@ -10,6 +10,7 @@
 
 #include "common.cuh"
 #include "ibcs.cuh"
+#include "tcgen05.cuh"
 
 namespace abx {
 
@@ -19,6 +20,22 @@ int* device_error_word() {
     void* ptr = nullptr;
     if (cudaGetSymbolAddress(&ptr, g_device_error) != cudaSuccess) return nullptr;
     return static_cast<int*>(ptr);
+}
+
+// One warp waits, bounded by limit_cycles, on an mbarrier that nothing arrives
+// at: the library's bounded wait gives up and the kernel records
+// ABX_ERR_DEVICE_TIMEOUT, exercising the timeout path without a fault.
+__global__ void wait_selftest_kernel(uint64_t limit_cycles, int* error) {
+    __shared__ __align__(8) uint64_t bar;
+    __shared__ int abort_flag;
+    if (threadIdx.x == 0) {
+        abort_flag = 0;
+        tc::mbar_init(smem_addr(&bar), 1);
+        tc::mbar_init_fence();
+    }
+    __syncwarp();
+    const bool ok = tc::mbar_wait_warp(smem_addr(&bar), 0, &abort_flag, limit_cycles);
+    if (!ok && threadIdx.x == 0) raise_device_error(error, ABX_ERR_DEVICE_TIMEOUT);
 }
 
 }  // namespace abx
@@ -407,6 +424,13 @@ int abx_cross_prefill(const void* q, int64_t q_tokens, const void* k, const void
                                           static_cast<const abx::bf16*>(text_v), text_tokens,
                                           static_cast<abx::bf16*>(o), lse, stream),
                       "prefill launch");
+}
+
+int abx_selftest_wait_timeout(int64_t limit_cycles, abx_stream_t stream) {
+    if (limit_cycles <= 0 || limit_cycles > 4000000000LL)
+        return fail(ABX_ERR_INVALID_ARGUMENT, "limit must be in (0, 4e9] cycles");
+    abx::wait_selftest_kernel<<<1, 32, 0, stream>>>(static_cast<uint64_t>(limit_cycles), abx::device_error_word());
+    return check_cuda(cudaGetLastError(), "self-test launch");
 }
 
 }  // extern "C"
