@@ -15,6 +15,7 @@
 
 #include "common.cuh"
 #include "ibcs.cuh"
+#include "tcgen05.cuh"
 
 namespace abx {
 namespace {
@@ -31,11 +32,38 @@ struct SumMaxOp {
 struct DenseScores {
     const float* scores;
     int64_t population;
-    __device__ __forceinline__ void prepare(int64_t) {}
+    __device__ __forceinline__ const float* row_ptr(int64_t row) const { return scores + row * population; }
     __device__ __forceinline__ float score(int64_t row, int j) const {
         return scores[row * population + j];
     }
 };
+
+constexpr uint64_t kSipWaitLimit = 400ull * 1000 * 1000;  // SM cycles (~0.2 s) for the row load
+
+// Smallest float f >= 1e-30f with RN(double(f) * s) >= 1. Multiplication by a
+// positive double rounds monotonically, so for every stored mass v (>= 1e-30f,
+// never NaN) the reference's test `double(v) * s >= 1` equals `v >= f`. Starts
+// from the rounded 1/s and steps one float at a time; false when s is not a
+// positive finite double or the steps do not settle.
+__device__ bool mark_threshold(double s, float& out) {
+    if (!(s > 0.0) || !isfinite(s)) return false;
+    float f = static_cast<float>(1.0 / s);
+    if (!(f >= 1e-30f)) f = 1e-30f;
+    for (int i = 0; i < 64 && f > 1e-30f; ++i) {
+        const float below = __int_as_float(__float_as_int(f) - 1);
+        if (static_cast<double>(below) * s >= 1.) f = below;
+        else break;
+    }
+    for (int i = 0; i < 64; ++i) {
+        if (static_cast<double>(f) * s >= 1.) {
+            out = f;
+            return true;
+        }
+        if (f == INFINITY) return false;
+        f = __int_as_float(__float_as_int(f) + 1);
+    }
+    return false;
+}
 
 using Reduce = cub::BlockReduce<SumMax, kSipThreads>;
 using CountScan = cub::BlockScan<int, kSipThreads>;
@@ -71,7 +99,7 @@ template <class Source>
 __global__ __launch_bounds__(kSipThreads) void sip_kernel(Source source, const float* __restrict__ offsets,
                                                           int32_t* __restrict__ sampled,
                                                           float* __restrict__ weights, int population,
-                                                          int samples) {
+                                                          int samples, int* device_error_word_ptr) {
     extern __shared__ __align__(16) double prefix[];
     Scratch& scratch = *reinterpret_cast<Scratch*>(prefix);
     __shared__ double scale;
@@ -79,6 +107,8 @@ __global__ __launch_bounds__(kSipThreads) void sip_kernel(Source source, const f
     __shared__ int added;
     __shared__ int last_residual;
     __shared__ int marking;
+    __shared__ int threshold_ok;
+    __shared__ float threshold;
 
     const int buckets = (population + kSipBucket - 1) / kSipBucket;
     float* values = reinterpret_cast<float*>(reinterpret_cast<unsigned char*>(prefix) + sip_prefix_region(population));
@@ -91,30 +121,55 @@ __global__ __launch_bounds__(kSipThreads) void sip_kernel(Source source, const f
     // iteration's partial sums. Every v_j is positive and its double is above
     // 1e-30, so the reference's `v > 0` test and fmax(v, 1e-30) are identities
     // here; the sums visit j = tid, tid + 256, ... in order as there.
-    source.prepare(row);
+    // The row's scores land in shared memory by one bulk copy (the whole row in
+    // flight at once); a ragged tail (or a row not 16-byte aligned) is loaded by
+    // the threads. Then v_j = max(score_j, 1e-30f) (csrc/sip.cu:58-59), fused
+    // with the first iteration's partial sums. Every v_j is positive and its
+    // double is above 1e-30, so the reference's `v > 0` test and fmax(v, 1e-30)
+    // are identities here; the sums visit j = tid, tid + 256, ... in order as
+    // there, and the max of the doubles is the double of the float max.
+    __shared__ __align__(8) uint64_t load_bar;
+    __shared__ int load_abort;
+    const float* src = source.row_ptr(row);
+    const int bulk = (reinterpret_cast<uintptr_t>(src) & 15) == 0 ? (population & ~3) : 0;
+    if (tid == 0) {
+        load_abort = 0;
+        tc::mbar_init(smem_addr(&load_bar), 1);
+        tc::mbar_init_fence();
+        if (bulk > 0) {
+            tc::mbar_arrive_expect_tx(smem_addr(&load_bar), static_cast<uint32_t>(bulk) * 4u);
+            tc::bulk_load(smem_addr(values), src, static_cast<uint32_t>(bulk) * 4u, smem_addr(&load_bar));
+        } else {
+            tc::mbar_arrive(smem_addr(&load_bar));
+        }
+    }
+    for (int j = bulk + tid; j < population; j += kSipThreads) values[j] = __ldg(src + j);
+    __syncthreads();
+    if (!tc::mbar_wait(smem_addr(&load_bar), 0, &load_abort, kSipWaitLimit))
+        raise_device_error(device_error_word_ptr, ABX_ERR_DEVICE_TIMEOUT);
     double local_sum = 0.;
     double local_max = 0.;
     {
+        float fmax_kept = 0.f;
         int j = tid;
         for (; j + (kLoadUnroll - 1) * kSipThreads < population; j += kLoadUnroll * kSipThreads) {
             float f[kLoadUnroll];
 #pragma unroll
-            for (int u = 0; u < kLoadUnroll; ++u) f[u] = fmaxf(source.score(row, j + u * kSipThreads), 1e-30f);
+            for (int u = 0; u < kLoadUnroll; ++u) f[u] = fmaxf(values[j + u * kSipThreads], 1e-30f);
 #pragma unroll
             for (int u = 0; u < kLoadUnroll; ++u) {
                 values[j + u * kSipThreads] = f[u];
-                const double value = static_cast<double>(f[u]);
-                local_sum += value;
-                local_max = fmax(local_max, value);
+                local_sum += static_cast<double>(f[u]);
+                fmax_kept = fmaxf(fmax_kept, f[u]);
             }
         }
         for (; j < population; j += kSipThreads) {
-            const float f = fmaxf(source.score(row, j), 1e-30f);
+            const float f = fmaxf(values[j], 1e-30f);
             values[j] = f;
-            const double value = static_cast<double>(f);
-            local_sum += value;
-            local_max = fmax(local_max, value);
+            local_sum += static_cast<double>(f);
+            fmax_kept = fmaxf(fmax_kept, f);
         }
+        local_max = static_cast<double>(fmax_kept);
     }
     if (tid == 0) certain = 0;
 
@@ -131,9 +186,46 @@ __global__ __launch_bounds__(kSipThreads) void sip_kernel(Source source, const f
             scale = (samples - certain) / total.sum;
             added = 0;
             marking = total.maximum * scale >= 1.0;
+            threshold_ok = marking && mark_threshold(scale, threshold);
         }
         __syncthreads();
-        if (marking) {
+        if (marking && threshold_ok) {
+            // mark <=> v >= threshold (exactly the reference's double test)
+            const float fs = threshold;
+            int count = 0;
+            local_sum = 0.;
+            float fmax_kept = 0.f;
+            int j = tid;
+            for (; j + (kMarkUnroll - 1) * kSipThreads < population; j += kMarkUnroll * kSipThreads) {
+                float f[kMarkUnroll];
+#pragma unroll
+                for (int u = 0; u < kMarkUnroll; ++u) f[u] = values[j + u * kSipThreads];
+#pragma unroll
+                for (int u = 0; u < kMarkUnroll; ++u) {
+                    const bool live = f[u] > 0.f;
+                    const bool mark = live && f[u] >= fs;
+                    if (mark) values[j + u * kSipThreads] = -f[u];
+                    count += mark;
+                    if (live && !mark) {
+                        local_sum += static_cast<double>(f[u]);
+                        fmax_kept = fmaxf(fmax_kept, f[u]);
+                    }
+                }
+            }
+            for (; j < population; j += kSipThreads) {
+                const float f = values[j];
+                const bool live = f > 0.f;
+                const bool mark = live && f >= fs;
+                if (mark) values[j] = -f;
+                count += mark;
+                if (live && !mark) {
+                    local_sum += static_cast<double>(f);
+                    fmax_kept = fmaxf(fmax_kept, f);
+                }
+            }
+            local_max = static_cast<double>(fmax_kept);
+            atomicAdd(&added, count);
+        } else if (marking) {
             const double s = scale;
             int count = 0;
             local_sum = 0.;
@@ -333,7 +425,8 @@ static cudaError_t launch_sip_impl(const Source& source, const float* offsets, i
                                            static_cast<int>(smem));
     if (err != cudaSuccess) return err;
     sip_kernel<Source><<<static_cast<unsigned>(rows), kSipThreads, smem, stream>>>(
-        source, offsets, ids, log_weights, static_cast<int>(population), static_cast<int>(samples));
+        source, offsets, ids, log_weights, static_cast<int>(population), static_cast<int>(samples),
+        device_error_word());
     return cudaGetLastError();
 }
 

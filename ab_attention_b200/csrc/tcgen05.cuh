@@ -248,6 +248,14 @@ __device__ __forceinline__ void tma_load_2d(uint32_t dst, const void* tmap, int3
 // ---- cp.async with zero fill -------------------------------------------------------------
 
 // Copies 16 bytes, or writes 16 zero bytes when `valid` is false (no global read).
+// Bulk copy of `bytes` (a multiple of 16; both addresses 16-byte aligned) from
+// global to this CTA's shared memory, completing on `bar` (byte count).
+__device__ __forceinline__ void bulk_load(uint32_t dst, const void* src, uint32_t bytes, uint32_t bar) {
+    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];\n"
+                 ::"r"(dst), "l"(src), "r"(bytes), "r"(bar)
+                 : "memory");
+}
+
 // Store a box from shared memory through a 3-D tensor map (bulk async group);
 // elements outside the tensor are not written.
 __device__ __forceinline__ void tma_store_3d(const void* tmap, uint32_t src, int32_t x, int32_t y, int32_t z) {
