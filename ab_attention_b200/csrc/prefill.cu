@@ -29,9 +29,9 @@
 //              row (zero fill).
 // TMEM: S/P double buffer in columns [0,128) and [128,256), O of group 0 in
 // [256,384), O of group 1 in [384,512).
-// Stages: a V stage is free only once PV of its tile has run, which follows the
-// tile's softmax, while a K stage frees as soon as S has run; so V gets three
-// stages and K two.
+// Stages: three for K and three for V (231.6 KB of shared memory with Q, just
+// under the 227 KB per-block limit); the gathers are issued as soon as a stage
+// frees, so deeper rings keep more of each operand in flight.
 // Registers: the launch gives every thread kLaunchRegs; the softmax warpgroups
 // then raise theirs to kSoftmaxRegs and the MMA/gather warpgroups lower theirs
 // to kProducerRegs (setmaxnreg). The split fits the launch's allocation
@@ -55,7 +55,7 @@ namespace {
 
 constexpr int kTileKeys = 128;
 constexpr int kTileGranules = kTileKeys / kKv4;
-constexpr int kKStages = 2;
+constexpr int kKStages = 3;
 constexpr int kVStages = 3;
 constexpr uint32_t kSlabBytes = 128 * 128;       // 128 rows x 64 bf16
 constexpr uint32_t kTileBytes = 2 * kSlabBytes;  // one 128 x 128 bf16 operand tile
@@ -108,6 +108,7 @@ constexpr uint32_t kOffTmemSlot = kOffBar + kNumBars * 8;
 constexpr uint32_t kOffAbort = kOffTmemSlot + 4;
 constexpr uint32_t kSmemUsed = kOffAbort + 4;
 constexpr uint32_t kSmemBytes = kSmemUsed + 1024;  // slack for aligning the base
+static_assert(kSmemBytes <= 227 * 1024, "shared memory exceeds the per-block limit");
 
 constexpr uint64_t kWaitLimit = 400ull * 1000 * 1000;  // SM cycles per wait (~0.2 s)
 constexpr float kRescaleThreshold = 8.0f;                // log2 units: rescale O when max grows > 2^8
