@@ -249,17 +249,18 @@ __global__ __launch_bounds__(256) void pool_kernel(const bf16* __restrict__ k, i
 //              reference's four lane classes, csrc/ibcs.cu:329-335,454-462),
 //              merged at the end as (c0 + c1) + (c2 + c3) (:468-477).
 //   warp 4     allocates and frees TMEM; one thread loads the 32 KB centroid
-//              tile once and 16 KB key tiles into a 3-stage ring (TMA), and
+//              tile once and 16 KB key tiles into a 2-stage ring (TMA), and
 //              issues the MMAs into two TMEM buffers.
 // Each epilogue warp stages its 32 rows x 32 blocks of fp16 per tile in shared
-// memory (64-byte swizzle, double-buffered) and writes them with one TMA store:
-// 64-byte row segments instead of 32 scattered 16-byte stores per instruction.
+// memory (64-byte swizzle) and writes them with one TMA store: 64-byte row
+// segments instead of 32 scattered 16-byte stores per instruction.
+// 74 KB of shared memory, 128 TMEM columns and 160 threads: three CTAs per SM.
 // ---------------------------------------------------------------------------
 
 constexpr int kLseRows = 128;                          // centroid rows per CTA = TMEM lanes
 constexpr int kLseTileBlocks = 32;                     // KV4 blocks per key tile
 constexpr int kLseTileKeys = kLseTileBlocks * kReps;  // 64 pooled rows = MMA N
-constexpr int kLseStages = 3;
+constexpr int kLseStages = 2;
 constexpr int kLseCtlWarp = 4;  // TMEM allocation, TMA and MMA issue
 constexpr int kLseThreads = 5 * 32;
 constexpr uint32_t kLseSlabA = kLseRows * 128;      // 128 rows x 64 bf16
@@ -269,8 +270,8 @@ constexpr uint32_t kLseOffA = 0;
 constexpr uint32_t kLseOffB = 2 * kLseSlabA;
 constexpr uint32_t kLseStageRowBytes = kLseTileBlocks * 2;                // 64 B of fp16 per row and tile
 constexpr uint32_t kLseOutBufBytes = 32 * kLseStageRowBytes;                // one warp's 32 rows
-constexpr uint32_t kLseOffOut = kLseOffB + kLseStages * kLseStageBytes;   // 4 warps x 2 buffers
-constexpr uint32_t kLseOffBar = kLseOffOut + 4 * 2 * kLseOutBufBytes;
+constexpr uint32_t kLseOffOut = kLseOffB + kLseStages * kLseStageBytes;   // one buffer per epilogue warp
+constexpr uint32_t kLseOffBar = kLseOffOut + 4 * kLseOutBufBytes;
 constexpr int kLseBarAFull = 0;
 constexpr int kLseBarBFull = 1;                            // kLseStages
 constexpr int kLseBarBEmpty = kLseBarBFull + kLseStages;  // kLseStages
@@ -417,7 +418,7 @@ __device__ __forceinline__ void lse_tile(const uint32_t (&acc)[32], int j0, int 
 }
 
 // grid (ceil(qb * 8 / 128), bh)
-__global__ __launch_bounds__(kLseThreads, 2) void lse_kernel(const __grid_constant__ LseMaps maps,
+__global__ __launch_bounds__(kLseThreads, 3) void lse_kernel(const __grid_constant__ LseMaps maps,
                                                              const LseArgs args) {
     extern __shared__ __align__(1024) unsigned char lse_smem[];
     const uint32_t raw = smem_addr(lse_smem);
@@ -550,10 +551,10 @@ __global__ __launch_bounds__(kLseThreads, 2) void lse_kernel(const __grid_consta
             const int j0 = t * kLseTileBlocks;
             const bool full = j0 + kLseTileBlocks <= args.fine_blocks;
             if (tma_out) {
-                // Staging buffer b of this warp: the store issued from it two tiles
-                // ago must have finished reading it.
-                const uint32_t buf = base + kLseOffOut + (warp * 2 + b) * kLseOutBufBytes;
-                if (lane == 0) tc::bulk_wait_read<1>();
+                // This warp's staging buffer: the store issued from it for the
+                // previous tile must have finished reading it.
+                const uint32_t buf = base + kLseOffOut + warp * kLseOutBufBytes;
+                if (lane == 0) tc::bulk_wait_read<0>();
                 __syncwarp();
                 const uint32_t row_addr = buf + lane * kLseStageRowBytes;
                 if (full) {
