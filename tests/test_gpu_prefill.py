@@ -139,3 +139,16 @@ def test_torch_ops_and_paged_attention_match_python_api():
     logw2 = torch.empty_like(logw)
     torch.ops.ab_attention.sip(scores, offsets, ids2, logw2)
     assert torch.equal(ids2, ids) and torch.equal(logw2, logw)
+
+
+def test_host_pipeline_equals_device_path():
+    """ab_attention_host (chunked copy-in / compute / copy-out) gives the device
+    path's result bit for bit, including a ragged last chunk."""
+    from ab_attention_b200 import ab_attention, ab_attention_host
+
+    q, k, v = (x.reshape(1, 5, -1, 128) for x in smooth_field(5, 2, 16, 32, seed=12, device="cuda"))
+    want = ab_attention(q, k, v, sample_pages=2, seed=7)
+    hq, hk, hv = (x.cpu().pin_memory() for x in (q, k, v))
+    got = ab_attention_host(hq, hk, hv, sample_pages=2, seed=7, heads_per_chunk=2)
+    assert got.device.type == "cpu"
+    assert torch.equal(got, want.cpu())
