@@ -46,30 +46,41 @@ __device__ __forceinline__ float tile_elem(const uint4* tile, int i, int d) {
 // way the reference's warp does it (csrc/ibcs.cu:143-151,173-181): lane p folds
 // dims p, p+32, p+64, p+96 in order, then the xor-butterfly 16,8,4,2,1 as seen
 // from lane 0.
+// The two bf16 of a 32-bit word as an f32x2 pair (low element in the low half).
+__device__ __forceinline__ uint64_t bf16x2_to_f32x2(uint32_t w) {
+    return (static_cast<uint64_t>(w & 0xffff0000u) << 32) | static_cast<uint64_t>(w << 16);
+}
+
 __device__ __forceinline__ float block_distance(const uint4* tile, int i, const float* center) {
-    float part[32];
+    // part[q] holds lane partials (2q, 2q + 1): packed f32x2 operations apply to
+    // each the same subtract and fused multiply-add, in the same order.
+    uint64_t part[16];
 #pragma unroll
-    for (int p = 0; p < 32; ++p) part[p] = 0.0f;
+    for (int q = 0; q < 16; ++q) part[q] = kZeros2;
 #pragma unroll
     for (int k = 0; k < 4; ++k) {
 #pragma unroll
         for (int c = 0; c < 4; ++c) {
             const uint4 raw = tile[chunk_slot(i, 4 * k + c)];
-            const bf16* vals = reinterpret_cast<const bf16*>(&raw);
+            const uint32_t w[4] = {raw.x, raw.y, raw.z, raw.w};
+            const float4 c0 = reinterpret_cast<const float4*>(center + 32 * k + 8 * c)[0];
+            const float4 c1 = reinterpret_cast<const float4*>(center + 32 * k + 8 * c)[1];
+            const uint64_t cp[4] = {pack2(c0.x, c0.y), pack2(c0.z, c0.w), pack2(c1.x, c1.y), pack2(c1.z, c1.w)};
 #pragma unroll
-            for (int e = 0; e < 8; ++e) {
-                const int p = c * 8 + e;
-                const float delta = __bfloat162float(vals[e]) - center[32 * k + p];
-                part[p] += delta * delta;
+            for (int h = 0; h < 4; ++h) {
+                const uint64_t delta = sub2(bf16x2_to_f32x2(w[h]), cp[h]);
+                part[4 * c + h] = fma2(delta, delta, part[4 * c + h]);
             }
         }
     }
+    // xor-butterfly 16, 8, 4, 2 on pairs, then 1
 #pragma unroll
-    for (int width = 16; width > 0; width >>= 1) {
+    for (int width = 8; width > 0; width >>= 1) {
 #pragma unroll
-        for (int p = 0; p < width; ++p) part[p] = part[p] + part[p + width];
+        for (int q = 0; q < width; ++q) part[q] = add2(part[q], part[q + width]);
     }
-    return part[0];
+    const float2 last = unpack2(part[0]);
+    return last.x + last.y;
 }
 
 // Block-wide argmax over one (value, index) per thread of a 128-thread block:
@@ -109,7 +120,7 @@ __global__ __launch_bounds__(128) void cluster_kernel(
     bf16* __restrict__ scaled, float* __restrict__ populations,
     int32_t* __restrict__ assignments, float kappa) {
     __shared__ uint4 tile[128 * 16];
-    __shared__ float center[kHeadDim];
+    __shared__ __align__(16) float center[kHeadDim];
     __shared__ int members[kQueryBlock];
     __shared__ float red_val[4];
     __shared__ int red_idx[4];
@@ -175,16 +186,22 @@ __global__ __launch_bounds__(128) void cluster_kernel(
     // (csrc/ibcs.cu:213-227); centroid = bf16_rn(sum / count) (:228-237).
     const int cluster = tid >> 4;
     const int chunk = tid & 15;
-    float acc[8];
-#pragma unroll
-    for (int e = 0; e < 8; ++e) acc[e] = 0.0f;
+    uint64_t acc2[4] = {kZeros2, kZeros2, kZeros2, kZeros2};  // dims (2h, 2h + 1) of the chunk
     for (int i = 0; i < n; ++i) {
         if (members[i] == cluster) {
             const uint4 raw = tile[chunk_slot(i, chunk)];
-            const bf16* vals = reinterpret_cast<const bf16*>(&raw);
-#pragma unroll
-            for (int e = 0; e < 8; ++e) acc[e] += __bfloat162float(vals[e]);
+            acc2[0] = add2(acc2[0], bf16x2_to_f32x2(raw.x));
+            acc2[1] = add2(acc2[1], bf16x2_to_f32x2(raw.y));
+            acc2[2] = add2(acc2[2], bf16x2_to_f32x2(raw.z));
+            acc2[3] = add2(acc2[3], bf16x2_to_f32x2(raw.w));
         }
+    }
+    float acc[8];
+#pragma unroll
+    for (int h = 0; h < 4; ++h) {
+        const float2 pair = unpack2(acc2[h]);
+        acc[2 * h] = pair.x;
+        acc[2 * h + 1] = pair.y;
     }
     const int count = counts[cluster];
     uint4 plain, pre;
