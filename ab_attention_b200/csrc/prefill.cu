@@ -146,6 +146,7 @@ struct PrefillArgs {
 struct PrefillMaps {
     CUtensorMap q;  // box 64 x 128 rows
     CUtensorMap kv[2][2];
+    CUtensorMap kv_dense[2];  // K, V of the head's tokens, box 64 x 128 rows (dense tiles)
 };
 
 // KV4 id of granule `slot` of this row (dense: the slot itself); -1 when the
@@ -291,6 +292,22 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const PrefillArgs 
                 use == 0 || tc::mbar_wait(bar(bar_empty + st), (use - 1) & 1, abort_flag, kWaitLimit);
             if (!__all_sync(0xffffffffu, free_ok)) break;
             issued = t + 1;
+            if (row_ids == nullptr && (t + 1) * kTileGranules <= args.samples) {
+                // Dense tile (granule id = slot): 128 consecutive rows, two 128-row
+                // boxes issued by the operand's first warp.
+                if (lane == 0) {
+                    const uint32_t bytes = part == 0 ? kTileBytes : 0u;
+                    tc::mbar_arrive_expect_tx(bar(bar_full + st), bytes);
+                    if (part == 0) {
+                        const int32_t y = static_cast<int32_t>(head * args.seq + t * kTileKeys);
+                        tc::tma_load_2d(ring + st * kTileBytes, &maps.kv_dense[op], 0, y, bar(bar_full + st));
+                        tc::tma_load_2d(ring + st * kTileBytes + kSlabBytes, &maps.kv_dense[op], 64, y,
+                                        bar(bar_full + st));
+                    }
+                }
+                __syncwarp();
+                continue;
+            }
             if (lane == 0) tc::mbar_arrive_expect_tx(bar(bar_full + st), warp_boxes * kBoxBytes);
             __syncwarp();
             bool text;
@@ -580,9 +597,11 @@ cudaError_t launch_prefill(const bf16* q, int64_t q_tokens, const bf16* k, const
     if (!has_video) sources[0][0] = sources[1][0] = has_text ? text_k : q;  // never read: no video slots
     const int64_t rows[2] = {has_video ? bh * seq : bh, has_text ? bh * text_tokens : rows_or(bh * seq, bh)};
     args.kv_rows = rows[0];  // first row past the video map: padding slots read zeros there
-    for (int op = 0; op < 2; ++op)
+    for (int op = 0; op < 2; ++op) {
         for (int src = 0; src < 2; ++src)
             if ((err = encode_rows(&maps.kv[op][src], sources[op][src], rows[src], kKv4)) != cudaSuccess) return err;
+        if ((err = encode_rows(&maps.kv_dense[op], sources[op][0], rows[0], kTileKeys)) != cudaSuccess) return err;
+    }
     err = cudaFuncSetAttribute(prefill_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                static_cast<int>(kSmemBytes));
     if (err != cudaSuccess) return err;
