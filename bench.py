@@ -102,8 +102,8 @@ class ClockSampler:
 
 # DRAM bytes (read + write) of one prefill launch per head at the Wan shape, from
 # one ncu capture of the 2-head case (dram__bytes_read.sum + dram__bytes_write.sum
-# = 136.10 + 24.86 MB); a head's K/V stay L2-resident, so traffic scales with heads.
-PREFILL_DRAM_BYTES_PER_HEAD = (136.10e6 + 24.86e6) / 2
+# = 135.95 + 25.51 MB); a head's K/V stay L2-resident, so traffic scales with heads.
+PREFILL_DRAM_BYTES_PER_HEAD = (135.95e6 + 25.51e6) / 2
 
 
 def plan_bytes(bh: int, tokens: int, samples: int) -> float:
