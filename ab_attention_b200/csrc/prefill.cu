@@ -16,7 +16,7 @@
 //              TMEM lane i (row max / sum need no shuffles); it streams S out of
 //              TMEM in 16-column chunks, writes P (bf16) back over S for the PV
 //              product and rescales its O lazily (only when its running max
-//              grows by more than 2^8). Group 1 hands (m, l) to group 0, which
+//              grows by more than 2^32). Group 1 hands (m, l) to group 0, which
 //              merges the two partial softmaxes into the output.
 //   warp  8    TMEM allocation + MMA issue (one thread): S(t) = Q K(t)^T with
 //              both operands in shared memory, O(t%2) += P(t) V(t) with P read
@@ -111,7 +111,10 @@ constexpr uint32_t kSmemBytes = kSmemUsed + 1024;  // slack for aligning the bas
 static_assert(kSmemBytes <= 227 * 1024, "shared memory exceeds the per-block limit");
 
 constexpr uint64_t kWaitLimit = 400ull * 1000 * 1000;  // SM cycles per wait (~0.2 s)
-constexpr float kRescaleThreshold = 8.0f;                // log2 units: rescale O when max grows > 2^8
+// log2 units: rescale O when the row max grows by more than 2^32. P is bf16 and
+// O, l are f32 (both with f32's exponent range), so P <= 2^32 and O, l stay
+// far from overflow; a large threshold makes rescales rare after the first tile.
+constexpr float kRescaleThreshold = 32.0f;
 
 constexpr uint32_t kIdescS = tc::idesc_bf16_f32(128, kTileKeys, 0, 0);  // Q, K both K-major
 constexpr uint32_t kIdescPV = tc::idesc_bf16_f32(128, 128, 0, 1);       // P K-major (TMEM), V MN-major
@@ -328,52 +331,53 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const PrefillArgs 
         __syncwarp();
     } else if (warp == kMmaWarp) {
         // ---- MMA issue ------------------------------------------------------------------------
-        if (lane == 0) {
-            bool ok = tc::mbar_wait(bar(kBarQFull), 0, abort_flag, kWaitLimit);
-            const uint32_t q_base = base + kOffQ;
+        // The whole warp runs this loop (warp-uniform operands); one elected lane issues.
+        {
+            bool ok = tc::mbar_wait_warp(bar(kBarQFull), 0, abort_flag, kWaitLimit);
+            const uint64_t qdesc0 = tc::smem_desc(base + kOffQ, 16, 1024, tc::kSwizzle128B);
             auto issue_pv = [&](int u) -> bool {
                 const int b = u & 1;
                 const int vst = u % kVStages;
-                if (!tc::mbar_wait(bar(kBarVFull + vst), (u / kVStages) & 1, abort_flag, kWaitLimit)) return false;
-                if (!tc::mbar_wait(bar(kBarPFull + b), (u >> 1) & 1, abort_flag, kWaitLimit)) return false;
+                if (!tc::mbar_wait_warp(bar(kBarVFull + vst), (u / kVStages) & 1, abort_flag, kWaitLimit)) return false;
+                if (!tc::mbar_wait_warp(bar(kBarPFull + b), (u >> 1) & 1, abort_flag, kWaitLimit)) return false;
                 tc::fence_after_sync();
-                const uint32_t v_base = base + kOffV + vst * kTileBytes;
+                const uint64_t vdesc0 =
+                    tc::smem_desc(base + kOffV + vst * kTileBytes, kSlabBytes, 1024, tc::kSwizzle128B);
 #pragma unroll
                 for (int j = 0; j < kTileKeys / 16; ++j) {
                     // 16 keys per step: P columns [8j, 8j+8); V rows [16j, 16j+16) (MN-major,
-                    // leading offset = the second 64-dim slab, stride offset = 8-row atom).
-                    const uint64_t bdesc = tc::smem_desc(v_base + j * 16 * 128, kSlabBytes, 1024, tc::kSwizzle128B);
-                    tc::mma_ts(tmem + col_o(b), tmem + col_s(b) + 8 * j, bdesc, kIdescPV, (u >= 2 || j > 0) ? 1u : 0u);
+                    // leading offset = the second 64-dim slab, stride offset = 8-row atom; the
+                    // descriptor's start field counts 16-byte units).
+                    tc::mma_ts_elect(tmem + col_o(b), tmem + col_s(b) + 8 * j, vdesc0 + ((j * 16 * 128) >> 4),
+                                     kIdescPV, (u >= 2 || j > 0) ? 1u : 0u);
                 }
-                tc::mma_commit(bar(kBarVEmpty + vst));
-                tc::mma_commit(bar(kBarPv + b));
+                tc::mma_commit_elect(bar(kBarVEmpty + vst));
+                tc::mma_commit_elect(bar(kBarPv + b));
                 return true;
             };
             for (int t = 0; ok && t < tiles; ++t) {
                 const int b = t & 1;
                 const int kst = t % kKStages;
-                if (!tc::mbar_wait(bar(kBarKFull + kst), (t / kKStages) & 1, abort_flag, kWaitLimit)) {
+                if (!tc::mbar_wait_warp(bar(kBarKFull + kst), (t / kKStages) & 1, abort_flag, kWaitLimit)) {
                     ok = false;
                     break;
                 }
-                const uint32_t k_base = base + kOffK + kst * kTileBytes;
+                const uint64_t kdesc0 = tc::smem_desc(base + kOffK + kst * kTileBytes, 16, 1024, tc::kSwizzle128B);
 #pragma unroll
                 for (int j = 0; j < 8; ++j) {
                     // 16 dims per step inside a 64-dim slab: advance the start by 32 bytes.
-                    const uint32_t off = (j >> 2) * kSlabBytes + (j & 3) * 32;
-                    const uint64_t adesc = tc::smem_desc(q_base + off, 16, 1024, tc::kSwizzle128B);
-                    const uint64_t bdesc = tc::smem_desc(k_base + off, 16, 1024, tc::kSwizzle128B);
-                    tc::mma_ss(tmem + col_s(b), adesc, bdesc, kIdescS, j > 0 ? 1u : 0u);
+                    const uint32_t off = ((j >> 2) * kSlabBytes + (j & 3) * 32) >> 4;
+                    tc::mma_ss_elect(tmem + col_s(b), qdesc0 + off, kdesc0 + off, kIdescS, j > 0 ? 1u : 0u);
                 }
-                tc::mma_commit(bar(kBarKEmpty + kst));
-                tc::mma_commit(bar(kBarSFull + b));
+                tc::mma_commit_elect(bar(kBarKEmpty + kst));
+                tc::mma_commit_elect(bar(kBarSFull + b));
                 if (t > 0 && !issue_pv(t - 1)) ok = false;
             }
             if (ok && !issue_pv(tiles - 1)) ok = false;
-            if (ok) tc::mma_commit(bar(kBarOFinal));
+            if (ok) tc::mma_commit_elect(bar(kBarOFinal));
             // Drain: every MMA issued above has completed before TMEM is freed.
-            tc::mma_commit(bar(kBarDrain));
-            tc::mbar_wait(bar(kBarDrain), 0, abort_flag, kWaitLimit, /*honor_abort=*/false);
+            tc::mma_commit_elect(bar(kBarDrain));
+            if (lane == 0) tc::mbar_wait(bar(kBarDrain), 0, abort_flag, kWaitLimit, /*honor_abort=*/false);
         }
         __syncwarp();
     } else {
@@ -431,7 +435,7 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const PrefillArgs 
             }
             const float tile_max = fmaxf(fmaxf(part_max[0], part_max[1]), fmaxf(part_max[2], part_max[3]));
             // Lazy rescale, decided per warp (tcgen05.ld/st are warp-collective):
-            // a row whose max grew by more than 2^8 moves its reference max and
+            // a row whose max grew by more than 2^32 moves its reference max and
             // scales its O row and sum; the other rows of the warp scale by 1.
             // O(g) holds PV of the group's earlier tiles, all complete: S(t) was
             // committed after them.
