@@ -23,7 +23,7 @@ CSRC = PKG / "csrc"
 BUILD = PKG / "_build"
 LIB = PKG / "libabx.so"
 SOURCES = ("ibcs.cu", "sip.cu", "prefill.cu", "capi.cu")
-HEADERS = ("common.cuh", "ibcs.cuh", "tcgen05.cuh", "tma_host.cuh", "f32x2.cuh")
+HEADERS = ("common.cuh", "ibcs.cuh", "tcgen05.cuh", "tma_host.cuh", "f32x2.cuh", "mix.cuh")
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 NVCC_FLAGS = [
     "-O3", "-std=c++17", "-lineinfo", "--use_fast_math", "-Xcompiler", "-fPIC",

@@ -270,16 +270,13 @@ int abx_build_plan(const void* q, const void* k, int64_t bh, int64_t seq, const 
     if (int st = check_sip_shape(l.rows, l.fine, samples)) return st;
     if (!offsets || !ids || !log_weights) return fail(ABX_ERR_INVALID_ARGUMENT, "plan buffers must be non-null");
     if (int st = run_ibcs_front(q, k, bh, seq, workspace, workspace_bytes, l, stream)) return st;
+    // SIP evaluates the mixture scores from the LSE rows itself (no score array).
     char* ws = static_cast<char*>(workspace);
-    float* scores = reinterpret_cast<float*>(ws + l.scores);
-    if (int st = check_cuda(abx::launch_mix(reinterpret_cast<const half*>(ws + l.lse), l.ld,
+    return check_cuda(abx::launch_sip_mixed(reinterpret_cast<const half*>(ws + l.lse), l.ld,
                                             reinterpret_cast<const float*>(ws + l.populations),
                                             reinterpret_cast<const float*>(ws + l.lse_max),
-                                            reinterpret_cast<const float*>(ws + l.lse_den), l.rows, l.fine, scores,
-                                            stream),
-                            "mix launch"))
-        return st;
-    return check_cuda(abx::launch_sip(scores, offsets, l.rows, l.fine, ids, log_weights, samples, stream),
+                                            reinterpret_cast<const float*>(ws + l.lse_den), offsets, l.rows, l.fine,
+                                            ids, log_weights, samples, stream),
                       "sip launch");
 }
 

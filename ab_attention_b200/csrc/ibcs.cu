@@ -18,6 +18,7 @@
 #include "common.cuh"
 #include "ibcs.cuh"
 #include "f32x2.cuh"
+#include "mix.cuh"
 #include "tcgen05.cuh"
 #include "tma_host.cuh"
 
@@ -663,19 +664,14 @@ __global__ __launch_bounds__(kMixThreads) void mix_kernel(const half* __restrict
 #pragma unroll
             for (int e = 0; e < kMixPerThread; ++e) value[c][e] = base[c * ld + min(e, last)];
     }
-    float total_weight = 0.0f;
-#pragma unroll
-    for (int c = 0; c < kCentroids; ++c) total_weight += row_weight[c];
+    const float total_weight = mix_total_weight(row_weight);
     float out[kMixPerThread];
 #pragma unroll
     for (int e = 0; e < kMixPerThread; ++e) {
-        float score = 0.0f;
+        half v[kCentroids];
 #pragma unroll
-        for (int c = 0; c < kCentroids; ++c) {
-            const float probability = exp2f(__half2float(value[c][e]) - row_max[c]) / row_den[c];
-            score += row_weight[c] * probability;
-        }
-        out[e] = score / total_weight;
+        for (int c = 0; c < kCentroids; ++c) v[c] = value[c][e];
+        out[e] = mix_score(v, row_max, row_den, row_weight, total_weight);
     }
     float* dst = scores + row * fine_blocks + j0;
     if (j0 + kMixPerThread <= fine_blocks && (reinterpret_cast<uintptr_t>(dst) & 15) == 0) {

@@ -22,6 +22,10 @@ size_t sip_smem_bytes(int64_t population);
 int sip_smem_limit();
 cudaError_t launch_sip(const float* scores, const float* offsets, int64_t rows, int64_t population,
                        int32_t* ids, float* log_weights, int64_t samples, cudaStream_t stream);
+// SIP fed by the IBCS centroid LSE rows (the mixture is evaluated in the kernel).
+cudaError_t launch_sip_mixed(const half* lse, int64_t ld, const float* populations, const float* lse_max,
+                             const float* lse_den, const float* offsets, int64_t rows, int64_t population,
+                             int32_t* ids, float* log_weights, int64_t samples, cudaStream_t stream);
 
 // Sparse / dense prefill.
 cudaError_t launch_prefill(const bf16* q, int64_t q_tokens, const bf16* k, const bf16* v, int64_t bh, int64_t seq,

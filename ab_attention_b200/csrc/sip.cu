@@ -8,13 +8,16 @@
 // same form so that --use_fast_math / fmad contraction produce the same
 // instructions.
 //
-// Scores come from a dense f32 [rows, population] array (the IBCS mixture of
-// build_plan, or the caller's scores for `_C.sip`).
+// Scores come from a dense f32 [rows, population] array (the caller's scores
+// for `_C.sip`), or, for build_plan, straight from the IBCS centroid LSE rows:
+// the kernel evaluates the mixture (mix.cuh, the scorer's own expression) into
+// shared memory while loading the row, so the score array is never written.
 #include <cub/block/block_reduce.cuh>
 #include <cub/block/block_scan.cuh>
 
 #include "common.cuh"
 #include "ibcs.cuh"
+#include "mix.cuh"
 #include "tcgen05.cuh"
 
 namespace abx {
@@ -30,11 +33,37 @@ struct SumMaxOp {
 };
 
 struct DenseScores {
+    static constexpr bool kDense = true;
     const float* scores;
     int64_t population;
     __device__ __forceinline__ const float* row_ptr(int64_t row) const { return scores + row * population; }
     __device__ __forceinline__ float score(int64_t row, int j) const {
         return scores[row * population + j];
+    }
+};
+
+// The IBCS centroid LSE rows of build_plan: fp16 [rows, kCentroids, ld]
+// (ld % 8 == 0, 16-byte aligned rows) with each (row, centroid)'s max, softmax
+// denominator and population.
+struct MixedScores {
+    static constexpr bool kDense = false;
+    const half* lse;
+    int64_t ld;
+    const float* populations;
+    const float* lse_max;
+    const float* lse_den;
+    // One block's score (the rare clamped-weight path), through the same function.
+    __device__ float score(int64_t row, int j) const {
+        float mx[kCentroids], den[kCentroids], weight[kCentroids];
+        half value[kCentroids];
+#pragma unroll
+        for (int c = 0; c < kCentroids; ++c) {
+            mx[c] = lse_max[row * kCentroids + c];
+            den[c] = lse_den[row * kCentroids + c];
+            weight[c] = populations[row * kCentroids + c];
+            value[c] = lse[(row * kCentroids + c) * ld + j];
+        }
+        return mix_score(value, mx, den, weight, mix_total_weight(weight));
     }
 };
 
@@ -128,25 +157,73 @@ __global__ __launch_bounds__(kSipThreads) void sip_kernel(Source source, const f
     // double is above 1e-30, so the reference's `v > 0` test and fmax(v, 1e-30)
     // are identities here; the sums visit j = tid, tid + 256, ... in order as
     // there, and the max of the doubles is the double of the float max.
-    __shared__ __align__(8) uint64_t load_bar;
-    __shared__ int load_abort;
-    const float* src = source.row_ptr(row);
-    const int bulk = (reinterpret_cast<uintptr_t>(src) & 15) == 0 ? (population & ~3) : 0;
-    if (tid == 0) {
-        load_abort = 0;
-        tc::mbar_init(smem_addr(&load_bar), 1);
-        tc::mbar_init_fence();
-        if (bulk > 0) {
-            tc::mbar_arrive_expect_tx(smem_addr(&load_bar), static_cast<uint32_t>(bulk) * 4u);
-            tc::bulk_load(smem_addr(values), src, static_cast<uint32_t>(bulk) * 4u, smem_addr(&load_bar));
-        } else {
-            tc::mbar_arrive(smem_addr(&load_bar));
+    if constexpr (Source::kDense) {
+        __shared__ __align__(8) uint64_t load_bar;
+        __shared__ int load_abort;
+        const float* src = source.row_ptr(row);
+        const int bulk = (reinterpret_cast<uintptr_t>(src) & 15) == 0 ? (population & ~3) : 0;
+        if (tid == 0) {
+            load_abort = 0;
+            tc::mbar_init(smem_addr(&load_bar), 1);
+            tc::mbar_init_fence();
+            if (bulk > 0) {
+                tc::mbar_arrive_expect_tx(smem_addr(&load_bar), static_cast<uint32_t>(bulk) * 4u);
+                tc::bulk_load(smem_addr(values), src, static_cast<uint32_t>(bulk) * 4u, smem_addr(&load_bar));
+            } else {
+                tc::mbar_arrive(smem_addr(&load_bar));
+            }
         }
+        for (int j = bulk + tid; j < population; j += kSipThreads) values[j] = __ldg(src + j);
+        __syncthreads();
+        if (!tc::mbar_wait(smem_addr(&load_bar), 0, &load_abort, kSipWaitLimit))
+            raise_device_error(device_error_word_ptr, ABX_ERR_DEVICE_TIMEOUT);
+    } else {
+        // Mixture scores of this row, 8 consecutive blocks per step (one 16-byte
+        // load per centroid; rows are padded to ld, so the last step stays inside).
+        __shared__ float mix_max[kCentroids], mix_den[kCentroids], mix_weight[kCentroids];
+        if (tid < kCentroids) {
+            mix_max[tid] = source.lse_max[row * kCentroids + tid];
+            mix_den[tid] = source.lse_den[row * kCentroids + tid];
+            mix_weight[tid] = source.populations[row * kCentroids + tid];
+        }
+        __syncthreads();
+        const float total_weight = mix_total_weight(mix_weight);
+        const half* base = source.lse + row * kCentroids * source.ld;
+        const int groups = (population + 7) / 8;
+        for (int g = tid; g < groups; g += 2 * kSipThreads) {
+            // two groups per pass: 16 loads in flight per thread
+            uint4 raw[2][kCentroids];
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+                const int gg = min(g + h * kSipThreads, groups - 1);
+#pragma unroll
+                for (int c = 0; c < kCentroids; ++c)
+                    raw[h][c] = __ldg(reinterpret_cast<const uint4*>(base + c * source.ld + 8 * gg));
+            }
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+                const int j0 = 8 * (g + h * kSipThreads);
+                if (j0 >= population) break;
+                float out[8];
+#pragma unroll
+                for (int e = 0; e < 8; ++e) {
+                    half v[kCentroids];
+#pragma unroll
+                    for (int c = 0; c < kCentroids; ++c) v[c] = reinterpret_cast<const half*>(&raw[h][c])[e];
+                    out[e] = mix_score(v, mix_max, mix_den, mix_weight, total_weight);
+                }
+                if (j0 + 8 <= population) {
+                    reinterpret_cast<float4*>(values + j0)[0] = make_float4(out[0], out[1], out[2], out[3]);
+                    reinterpret_cast<float4*>(values + j0)[1] = make_float4(out[4], out[5], out[6], out[7]);
+                } else {
+#pragma unroll
+                    for (int e = 0; e < 8; ++e)
+                        if (j0 + e < population) values[j0 + e] = out[e];
+                }
+            }
+        }
+        __syncthreads();
     }
-    for (int j = bulk + tid; j < population; j += kSipThreads) values[j] = __ldg(src + j);
-    __syncthreads();
-    if (!tc::mbar_wait(smem_addr(&load_bar), 0, &load_abort, kSipWaitLimit))
-        raise_device_error(device_error_word_ptr, ABX_ERR_DEVICE_TIMEOUT);
     double local_sum = 0.;
     double local_max = 0.;
     {
@@ -433,6 +510,14 @@ static cudaError_t launch_sip_impl(const Source& source, const float* offsets, i
 cudaError_t launch_sip(const float* scores, const float* offsets, int64_t rows, int64_t population,
                        int32_t* ids, float* log_weights, int64_t samples, cudaStream_t stream) {
     DenseScores source{scores, population};
+    return launch_sip_impl(source, offsets, rows, population, ids, log_weights, samples, stream);
+}
+
+cudaError_t launch_sip_mixed(const half* lse, int64_t ld, const float* populations, const float* lse_max,
+                             const float* lse_den, const float* offsets, int64_t rows, int64_t population,
+                             int32_t* ids, float* log_weights, int64_t samples, cudaStream_t stream) {
+    if (ld % 8 != 0 || ld < population || (reinterpret_cast<uintptr_t>(lse) & 15) != 0) return cudaErrorInvalidValue;
+    const MixedScores source{lse, ld, populations, lse_max, lse_den};
     return launch_sip_impl(source, offsets, rows, population, ids, log_weights, samples, stream);
 }
 

@@ -144,3 +144,23 @@ def test_plan_properties_at_full_size():
     first_residual = (~certain).int().argmax(dim=1)
     pos = torch.arange(ids.shape[1], device=ids.device)[None, :]
     assert bool((certain == (pos < first_residual[:, None])).all())
+
+
+@pytest.mark.parametrize("bh,grid,pages", [(2, (3, 16, 43), 4), (1, (1, 7, 148), 8)])
+def test_build_plan_equals_scores_then_sip(bh, grid, pages):
+    """build_plan's SIP evaluates the mixture from the LSE rows itself; its plan is
+    bit-identical to scoring first (ops.ibcs) and sampling those scores (ops.sip)."""
+    from ab_attention_b200.synthetic import smooth_field
+    q, k, _ = smooth_field(bh, *grid, seed=21, sigma=0.2, device="cuda")
+    q4, k4 = q.unsqueeze(0), k.unsqueeze(0)
+    tokens = q.shape[1]
+    qb = -(-tokens // 128)
+    gen = torch.Generator(device="cuda").manual_seed(8)
+    offsets = torch.rand(bh * qb, device="cuda", generator=gen)
+    plan = build_plan(q4, k4, sample_pages=pages, offsets=offsets)
+    scores = ops.ibcs(q4, k4)
+    ids = torch.empty((bh * qb, pages * 32), dtype=torch.int32, device="cuda")
+    logw = torch.empty_like(ids, dtype=torch.float32)
+    ops.sip(scores, offsets, ids, logw)
+    np.testing.assert_array_equal(plan.descriptor.reshape(bh * qb, -1).cpu().numpy(), ids.cpu().numpy())
+    np.testing.assert_array_equal(plan.log_weights.reshape(bh * qb, -1).cpu().numpy(), logw.cpu().numpy())
