@@ -102,8 +102,8 @@ class ClockSampler:
 
 # DRAM bytes (read + write) of one prefill launch per head at the Wan shape, from
 # one ncu capture of the 2-head case (dram__bytes_read.sum + dram__bytes_write.sum
-# = 135.95 + 25.51 MB); a head's K/V stay L2-resident, so traffic scales with heads.
-PREFILL_DRAM_BYTES_PER_HEAD = (135.95e6 + 25.51e6) / 2
+# = 136.00 + 25.44 MB); a head's K/V stay L2-resident, so traffic scales with heads.
+PREFILL_DRAM_BYTES_PER_HEAD = (136.00e6 + 25.44e6) / 2
 
 
 def plan_bytes(bh: int, tokens: int, samples: int) -> float:
@@ -446,15 +446,15 @@ def main() -> None:
                      "frac": achieved / peaks["bf16_tflops_sustained"],
                      "traffic": (PREFILL_DRAM_BYTES_PER_HEAD * per if shape.name.startswith("wan14b") else None),
                      "peak_source": peaks["source"] + " sustained bf16"},
-        "plan_roofline": {"kernels": "cluster+pool+lse+mix+sip", "bound": "hbm",
+        "plan_roofline": {"kernels": "cluster+pool+lse+sip (mixture evaluated inside sip)", "bound": "hbm",
                           "achieved": plan_bytes(per, tokens, shape.sample_pages * 32) / (plan_ms * 1e-3) / 1e9,
                           "peak": peaks["hbm_gbs"], "unit": "GB/s",
                           "frac": plan_bytes(per, tokens, shape.sample_pages * 32) / (plan_ms * 1e-3) / 1e9
                           / peaks["hbm_gbs"],
                           "note": "algorithmic bytes (Q, K in; plan out); the kernels are bound by the exact "
                                   "fast-math exp2/log2/division work and the double-precision SIP sums"},
-        # cluster, pool, lse, mix, sip + one prefill per head block per step (NCCL's kernels not counted)
-        "gpu_launches": (5 + chunks) * args.steps,
+        # cluster, pool, lse, sip + one prefill per head block per step (NCCL's kernels not counted)
+        "gpu_launches": (4 + chunks) * args.steps,
         "clocks": clocks.summary(),
         **dense,
     }
