@@ -253,6 +253,8 @@ def main() -> None:
     parser.add_argument("--no-cpu-baseline", action="store_true")
     parser.add_argument("--no-dense", action="store_true")
     parser.add_argument("--no-e2e", action="store_true")
+    parser.add_argument("--sample-pages", type=int, default=0,
+                        help="override the configuration's sampled pages per row (the C4 sweep: 16..256)")
     parser.add_argument("--bh", type=int, default=0,
                         help="run only the first BH (batch*head) rows of the configuration (profiling)")
     args = parser.parse_args()
@@ -260,6 +262,10 @@ def main() -> None:
     from ab_attention_b200.synthetic import CONFIGS, make_inputs
 
     shape = CONFIGS[args.config]
+    if args.sample_pages:
+        import dataclasses
+
+        shape = dataclasses.replace(shape, name=f"{shape.name}[p={args.sample_pages}]", sample_pages=args.sample_pages)
     if args.bh:
         import dataclasses
 
@@ -444,7 +450,9 @@ def main() -> None:
         "roofline": {"kernel": "sparse prefill", "bound": "tensor", "achieved": achieved,
                      "peak": peaks["bf16_tflops_sustained"], "unit": "TFLOP/s",
                      "frac": achieved / peaks["bf16_tflops_sustained"],
-                     "traffic": (PREFILL_DRAM_BYTES_PER_HEAD * per if shape.name.startswith("wan14b") else None),
+                     # the per-head figure was captured at the wan14b shape with 64 pages
+                     "traffic": (PREFILL_DRAM_BYTES_PER_HEAD * per
+                                 if shape.name.split("[")[0] == "wan14b" and shape.sample_pages == 64 else None),
                      "peak_source": peaks["source"] + " sustained bf16"},
         "plan_roofline": {"kernels": "cluster+pool+lse+sip (mixture evaluated inside sip)", "bound": "hbm",
                           "achieved": plan_bytes(per, tokens, shape.sample_pages * 32) / (plan_ms * 1e-3) / 1e9,
