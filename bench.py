@@ -283,7 +283,19 @@ def main() -> None:
     torch.cuda.set_device(local)
     device = torch.device("cuda", local)
     if world > 1:
-        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=device)
+        # NCCL prints its version banner on stdout while it creates the communicator;
+        # route it to stderr so that rank 0's stdout carries only the JSON line.
+        sys.stdout.flush()
+        saved_stdout = os.dup(1)
+        try:
+            os.dup2(2, 1)
+            dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=device)
+            dist.barrier(device_ids=[local])
+            torch.cuda.synchronize()
+        finally:
+            sys.stdout.flush()
+            os.dup2(saved_stdout, 1)
+            os.close(saved_stdout)
     from ab_attention_b200 import shard
 
     bh = shape.batch_heads
