@@ -22,7 +22,7 @@ ROOT = PKG.parent
 CSRC = PKG / "csrc"
 BUILD = PKG / "_build"
 LIB = PKG / "libabx.so"
-SOURCES = ("ibcs.cu", "sip.cu", "prefill.cu", "capi.cu")
+SOURCES = ("ibcs.cu", "sip.cu", "prefill.cu", "prefill_pair.cu", "capi.cu")
 HEADERS = ("common.cuh", "ibcs.cuh", "tcgen05.cuh", "tma_host.cuh", "f32x2.cuh", "mix.cuh")
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 NVCC_FLAGS = [

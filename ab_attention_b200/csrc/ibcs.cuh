@@ -33,4 +33,13 @@ cudaError_t launch_prefill(const bf16* q, int64_t q_tokens, const bf16* k, const
                            const bf16* text_k, const bf16* text_v, int64_t text_tokens, bf16* o,
                            float* lse, cudaStream_t stream);
 
+// Paired sparse prefill (two adjacent query blocks per CTA over the union of
+// their samples); pair_supported() says whether a shape can take it.
+bool pair_supported(int64_t seq, int64_t samples, int64_t text_tokens);
+size_t pair_workspace_bytes(int64_t bh, int64_t seq, int64_t samples, int64_t text_tokens);
+cudaError_t launch_prefill_pair(const bf16* q, const bf16* k, const bf16* v, int64_t bh, int64_t seq,
+                                const int32_t* ids, const float* log_weights, int64_t samples, const bf16* text_k,
+                                const bf16* text_v, int64_t text_tokens, bf16* o, float* lse, void* workspace,
+                                size_t workspace_bytes, cudaStream_t stream);
+
 }  // namespace abx

@@ -257,10 +257,11 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const PrefillArgs 
     tc::fence_after_sync();
     const uint32_t tmem = *tmem_slot;
 
-    // Register split by warpgroup (every warp of a warpgroup executes the same one).
-    if (warp < kMmaWarp) asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;\n" ::"n"(kSoftmaxRegs));
-    else asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;\n" ::"n"(kProducerRegs));
-
+    // Register split by warpgroup: each warpgroup executes one setmaxnreg, and each
+    // role's code sits under its own (no merge in between, so the compiler gives
+    // the softmax code the raised count).
+    if (warp >= kMmaWarp) {
+    asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;\n" ::"n"(kProducerRegs));
     if (warp >= kKLoadWarp) {
         // ---- producers: one TMA box per lane per operand tile --------------------------------
         const bool is_k = warp < kVLoadWarp;
@@ -380,7 +381,9 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const PrefillArgs 
             if (lane == 0) tc::mbar_wait(bar(kBarDrain), 0, abort_flag, kWaitLimit, /*honor_abort=*/false);
         }
         __syncwarp();
+    }
     } else {
+        asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;\n" ::"n"(kSoftmaxRegs));
         // ---- softmax group g (thread = query row = TMEM lane) ---------------------------------------
         const int g = warp >> 2;
         const int r = tid & 127;  // query row

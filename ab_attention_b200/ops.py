@@ -159,8 +159,13 @@ def build_plan_into(q3: torch.Tensor, k3: torch.Tensor, offsets: torch.Tensor, i
                                       _lib.stream_of(q3)), "abx_build_plan")
 
 
-def sparse_prefill(q3, k3, v3, ids, logw, *, text_k=None, text_v=None, return_lse=False):
-    """HT-weighted sparse prefill over [BH,S,128] bf16 q/k/v; ids/logw [rows, samples]."""
+def sparse_prefill(q3, k3, v3, ids, logw, *, text_k=None, text_v=None, return_lse=False, paired=True):
+    """HT-weighted sparse prefill over [BH,S,128] bf16 q/k/v; ids/logw [rows, samples].
+
+    ``paired`` (default) serves two adjacent query blocks per CTA from one gather
+    of the union of their samples (abx_sparse_prefill_paired); False runs one
+    query block per CTA (abx_sparse_prefill). Both compute the same attention.
+    """
     bh, seq, _ = q3.shape
     samples = ids.shape[-1]
     o = torch.empty_like(q3)
@@ -168,9 +173,22 @@ def sparse_prefill(q3, k3, v3, ids, logw, *, text_k=None, text_v=None, return_ls
     text_tokens = 0 if text_k is None else text_k.shape[1]
     lib = _lib.load()
     with torch.cuda.device(q3.device):
-        _lib.check(lib.abx_sparse_prefill(_lib.ptr(q3), _lib.ptr(k3), _lib.ptr(v3), bh, seq, _lib.ptr(ids),
-                                          _lib.ptr(logw), samples, _lib.ptr(text_k), _lib.ptr(text_v), text_tokens,
-                                          _lib.ptr(o), _lib.ptr(lse_), _lib.stream_of(q3)), "abx_sparse_prefill")
+        ws_bytes = ctypes.c_size_t(0)
+        if paired:
+            _lib.check(lib.abx_prefill_workspace_size(bh, seq, samples, text_tokens, ctypes.byref(ws_bytes)),
+                       "abx_prefill_workspace_size")
+        if ws_bytes.value:
+            ws = torch.empty(ws_bytes.value, dtype=torch.uint8, device=q3.device)
+            _lib.check(lib.abx_sparse_prefill_paired(_lib.ptr(q3), _lib.ptr(k3), _lib.ptr(v3), bh, seq,
+                                                     _lib.ptr(ids), _lib.ptr(logw), samples, _lib.ptr(text_k),
+                                                     _lib.ptr(text_v), text_tokens, _lib.ptr(o), _lib.ptr(lse_),
+                                                     _lib.ptr(ws), ws_bytes.value, _lib.stream_of(q3)),
+                       "abx_sparse_prefill_paired")
+        else:
+            _lib.check(lib.abx_sparse_prefill(_lib.ptr(q3), _lib.ptr(k3), _lib.ptr(v3), bh, seq, _lib.ptr(ids),
+                                              _lib.ptr(logw), samples, _lib.ptr(text_k), _lib.ptr(text_v),
+                                              text_tokens, _lib.ptr(o), _lib.ptr(lse_), _lib.stream_of(q3)),
+                       "abx_sparse_prefill")
     return o, lse_
 
 

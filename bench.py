@@ -473,8 +473,9 @@ def main() -> None:
                           / peaks["hbm_gbs"],
                           "note": "algorithmic bytes (Q, K in; plan out); the kernels are bound by the exact "
                                   "fast-math exp2/log2/division work and the double-precision SIP sums"},
-        # cluster, pool, lse, sip + one prefill per head block per step (NCCL's kernels not counted)
-        "gpu_launches": (4 + chunks) * args.steps,
+        # cluster, pool, lse, sip + a pair plan and a prefill per head block per step
+        # (NCCL's kernels not counted)
+        "gpu_launches": (4 + 2 * chunks) * args.steps,
         "clocks": clocks.summary(),
         **dense,
     }

@@ -141,6 +141,20 @@ int abx_sparse_prefill(const void* q, const void* k, const void* v, int64_t bh, 
                        const void* text_k, const void* text_v, int64_t text_tokens,
                        void* o, float* lse, abx_stream_t stream);
 
+/* abx_sparse_prefill with two adjacent query blocks of a head per CTA, fed from
+ * one gather of the union of their samples (same results up to the order of
+ * the floating-point sums). `workspace` (device memory, any alignment) holds the
+ * per-pair union lists; abx_prefill_workspace_size() gives its size, 0 when the
+ * shape cannot be paired (more than 65,534 slots, or a map of seq/4 slots
+ * larger than shared memory), in which case this call is abx_sparse_prefill and
+ * ignores the workspace. Same replaced interface as abx_sparse_prefill. */
+int abx_prefill_workspace_size(int64_t bh, int64_t seq, int64_t samples, int64_t text_tokens, size_t* bytes);
+int abx_sparse_prefill_paired(const void* q, const void* k, const void* v, int64_t bh, int64_t seq,
+                              const int32_t* ids, const float* log_weights, int64_t samples,
+                              const void* text_k, const void* text_v, int64_t text_tokens,
+                              void* o, float* lse, void* workspace, size_t workspace_bytes,
+                              abx_stream_t stream);
+
 /* Dense attention through the same prefill kernel (every KV4 block, shift 0):
  * the dense comparator. o / lse as above. */
 int abx_dense_prefill(const void* q, const void* k, const void* v, int64_t bh, int64_t seq,
