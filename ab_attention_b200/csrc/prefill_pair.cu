@@ -11,7 +11,7 @@
 //
 // Pair plan (pair_plan_kernel, one CTA per pair): the union as a list of
 // entries (16-bit slot of A | 16-bit slot of B << 16; 0xFFFF = not sampled by
-// that row; slots >= samples are text granules), laid out in tiles of 16
+// that row; slots >= samples are text granules), laid out in tiles of 32
 // granules (128 keys):
 //   [shared granules | text granules | padding]  tiles both rows attend to,
 //   then tiles holding only A's or only B's granules, alternating A, B, A, B
@@ -126,22 +126,31 @@ __global__ void __launch_bounds__(kPlanThreads) pair_plan_kernel(const PairPlanA
     const int n = a.samples;
     const int fine = a.fine_blocks;
 
-    int* slot_of_b = reinterpret_cast<int*>(plan_smem);                       // [fine]
-    uint32_t* seen_a = reinterpret_cast<uint32_t*>(slot_of_b + fine);         // [ceil(fine / 32)]
+    // B's slot of each granule (16-bit, kNoSlot = not sampled by B), bitmaps of the
+    // granules seen in A and in B (repeated ids), and B's slots matched by A.
     const int seen_words = (fine + 31) / 32;
-    uint8_t* used_b = reinterpret_cast<uint8_t*>(seen_a + seen_words);        // [samples]
+    const int map_words = (fine + 1) / 2;
+    uint16_t* slot_of_b = reinterpret_cast<uint16_t*>(plan_smem);                  // [2 * map_words]
+    uint32_t* seen_a = reinterpret_cast<uint32_t*>(plan_smem) + map_words;         // [seen_words]
+    uint32_t* seen_b = seen_a + seen_words;                                         // [seen_words]
+    uint8_t* used_b = reinterpret_cast<uint8_t*>(seen_b + seen_words);              // [samples]
     __shared__ int warp_sums[kPlanWarps];
 
-    for (int i = threadIdx.x; i < fine; i += kPlanThreads) slot_of_b[i] = -1;
-    for (int i = threadIdx.x; i < seen_words; i += kPlanThreads) seen_a[i] = 0;
+    for (int i = threadIdx.x; i < map_words; i += kPlanThreads) reinterpret_cast<uint32_t*>(plan_smem)[i] = ~0u;
+    for (int i = threadIdx.x; i < 2 * seen_words; i += kPlanThreads) seen_a[i] = 0;
     for (int i = threadIdx.x; i < n; i += kPlanThreads) used_b[i] = 0;
     __syncthreads();
     bool bad = false;
     if (has_b) {
         for (int s = threadIdx.x; s < n; s += kPlanThreads) {
             const int id = __ldg(ids_b + s);
-            if (id < 0 || id >= fine) bad = true;
-            else if (atomicExch(slot_of_b + id, s) != -1) bad = true;  // repeated id in B
+            if (id < 0 || id >= fine) {
+                bad = true;
+                continue;
+            }
+            const uint32_t bit = 1u << (id & 31);
+            if (atomicOr(seen_b + (id >> 5), bit) & bit) bad = true;  // repeated id in B
+            slot_of_b[id] = static_cast<uint16_t>(s);
         }
     }
     __syncthreads();
@@ -153,8 +162,8 @@ __global__ void __launch_bounds__(kPlanThreads) pair_plan_kernel(const PairPlanA
         }
         const uint32_t bit = 1u << (id & 31);
         if (atomicOr(seen_a + (id >> 5), bit) & bit) bad = true;  // repeated id in A
-        const int sb = slot_of_b[id];
-        if (sb >= 0) used_b[sb] = 1;
+        const uint32_t sb = slot_of_b[id];
+        if (sb != kNoSlot) used_b[sb] = 1;
     }
     bad = __syncthreads_or(bad);
 
@@ -164,7 +173,7 @@ __global__ void __launch_bounds__(kPlanThreads) pair_plan_kernel(const PairPlanA
     const int s1 = min(n, s0 + chunk);
     int my_shared = 0, my_b_only = 0;
     for (int s = s0; s < s1; ++s) {
-        if (!bad && has_b && slot_of_b[__ldg(ids_a + s)] >= 0) ++my_shared;
+        if (!bad && has_b && slot_of_b[__ldg(ids_a + s)] != kNoSlot) ++my_shared;
         if (has_b && (bad || !used_b[s])) ++my_b_only;
     }
     int n_shared, n_b_only;
@@ -184,7 +193,8 @@ __global__ void __launch_bounds__(kPlanThreads) pair_plan_kernel(const PairPlanA
     int shared_idx = shared_before;
     int b_idx = b_only_before;
     for (int s = s0; s < s1; ++s) {
-        const int sb = (!bad && has_b) ? slot_of_b[__ldg(ids_a + s)] : -1;
+        const uint32_t sb_raw = (!bad && has_b) ? slot_of_b[__ldg(ids_a + s)] : kNoSlot;
+        const int sb = sb_raw == kNoSlot ? -1 : static_cast<int>(sb_raw);
         const int id_a = video_code(__ldg(ids_a + s));
         if (sb >= 0) {
             code[shared_idx] = id_a;
@@ -714,7 +724,8 @@ int64_t pair_stride(int64_t samples, int64_t text_granules) {
 }
 
 size_t plan_smem_bytes(int64_t fine_blocks, int64_t samples) {
-    return static_cast<size_t>(fine_blocks) * 4 + static_cast<size_t>(ceil_div(fine_blocks, 32)) * 4 +
+    // 16-bit slot map (rounded to words), two bitmaps, one byte per sample
+    return static_cast<size_t>(ceil_div(fine_blocks, 2)) * 4 + static_cast<size_t>(ceil_div(fine_blocks, 32)) * 8 +
            static_cast<size_t>(samples);
 }
 
