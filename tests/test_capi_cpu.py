@@ -102,3 +102,28 @@ def test_cross_prefill_validates_before_launch():
     # no keys at all; negative text count
     assert lib.abx_cross_prefill(p, 10, None, None, 0, 1, None, None, 0, None, None, 0, p, None, None) == 1
     assert lib.abx_cross_prefill(p, 10, p, p, 8, 1, None, None, 2, p, p, -1, p, None, None) == 1
+
+
+def test_paired_prefill_workspace_and_validation():
+    """abx_prefill_workspace_size sizes the pair lists (0 when a shape cannot be
+    paired); abx_sparse_prefill_paired refuses a missing or short workspace
+    before any launch."""
+    lib = _lib.load()
+    out = ctypes.c_size_t(0)
+    bh, seq, samples = 80, 75600, 2048
+    assert lib.abx_prefill_workspace_size(bh, seq, samples, 0, ctypes.byref(out)) == 0
+    pairs = bh * ((591 + 1) // 2)
+    per_pair = (2 * samples + 3 * 32 + 31) // 32 * 32 * 8  # entries + granule codes, 4 bytes each (32-granule tiles)
+    assert pairs * per_pair <= out.value <= pairs * per_pair + pairs * 16 + 4096
+    with_text = ctypes.c_size_t(0)
+    assert lib.abx_prefill_workspace_size(bh, seq, samples, 256, ctypes.byref(with_text)) == 0
+    assert with_text.value > out.value  # the text granules join every pair's list
+    assert lib.abx_prefill_workspace_size(bh, seq, 0, 0, ctypes.byref(out)) == 0 and out.value == 0  # nothing to pair
+    assert lib.abx_prefill_workspace_size(0, seq, samples, 0, ctypes.byref(out)) == 1
+    assert lib.abx_prefill_workspace_size(bh, seq, -1, 0, ctypes.byref(out)) == 1
+    p = ctypes.c_void_p(16)  # never dereferenced: validation fails first
+    assert lib.abx_sparse_prefill_paired(p, p, p, 1, 1024, p, p, 8, None, None, 0, p, None, None, 0, None) == 3
+    assert lib.abx_sparse_prefill_paired(p, p, p, 1, 1024, p, p, 8, None, None, 0, p, None, p, 64, None) == 3
+    assert lib.abx_sparse_prefill_paired(p, p, p, 1, 1024, p, None, 8, None, None, 0, p, None, p, 1 << 30, None) == 1
+    assert lib.abx_sparse_prefill_paired(ctypes.c_void_p(18), p, p, 1, 1024, p, p, 8, None, None, 0, p, None, p,
+                                         1 << 30, None) == 1
