@@ -47,7 +47,9 @@ def measured_peaks() -> dict:
 
 
 class ClockSampler:
-    """Samples nvidia-smi SM clocks and throttle reasons during the timed region."""
+    """Samples nvidia-smi SM clocks and throttle reasons every 20 ms. It is started
+    before the warm-up (nvidia-smi takes a moment to start) and keeps only the
+    samples that arrive inside the timed window (`mark_start` .. `mark_stop`)."""
 
     FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
@@ -56,13 +58,14 @@ class ClockSampler:
     def __init__(self, index: int):
         self.index = index
         self.proc = None
-        self.lines: list[str] = []
+        self.lines: list[tuple[float, str]] = []
+        self.window = (0.0, float("inf"))
 
     def __enter__(self):
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
-                 "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+                 "-lms", "20"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
             self.thread = threading.Thread(target=self._read, daemon=True)
             self.thread.start()
         except OSError:
@@ -71,7 +74,13 @@ class ClockSampler:
 
     def _read(self):
         for line in self.proc.stdout:
-            self.lines.append(line.strip())
+            self.lines.append((time.monotonic(), line.strip()))
+
+    def mark_start(self):
+        self.window = (time.monotonic(), float("inf"))
+
+    def mark_stop(self):
+        self.window = (self.window[0], time.monotonic() + 0.025)  # a sample in flight at the end
 
     def __exit__(self, *exc):
         if self.proc is not None:
@@ -84,7 +93,10 @@ class ClockSampler:
     def summary(self) -> dict:
         sm, mx, reasons = [], None, set()
         names = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
-        for line in self.lines:
+        lo, hi = self.window
+        for when, line in self.lines:
+            if not lo <= when <= hi:
+                continue
             parts = [p.strip() for p in line.split(",")]
             if len(parts) < 9:
                 continue
@@ -339,18 +351,20 @@ def main() -> None:
             e[2].record(stream)
         return o
 
-    for _ in range(max(3, args.warmup)):
-        step()
-    torch.cuda.synchronize()
-    barrier()
-    torch.cuda.synchronize()
     start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with ClockSampler(local) as clocks:
+        for _ in range(max(3, args.warmup)):
+            step()
+        torch.cuda.synchronize()
+        barrier()
+        torch.cuda.synchronize()
+        clocks.mark_start()
         start.record(stream)
         for i in range(args.steps):
             step(i)
         stop.record(stream)
         torch.cuda.synchronize()
+        clocks.mark_stop()
     barrier()
     elapsed = start.elapsed_time(stop)
     if world > 1:
