@@ -107,7 +107,8 @@ def test_rank_heads_partition_every_head_once():
     for world, chunks in [(1, 1), (2, 4), (4, 2), (8, 1)]:
         owned = sorted(h for r in range(world) for h in shard.rank_heads(BH, world, r, chunks))
         assert owned == list(range(BH))
-    assert shard.chunk_count(80, 8) == 2 and shard.chunk_count(80, 2) == 4 and shard.chunk_count(24, 8) == 3
+    assert shard.chunk_count(80, 8) == 5 and shard.chunk_count(80, 2) == 8 and shard.chunk_count(24, 8) == 3
+    assert shard.chunk_count(80, 8, max_chunks=4) == 2
     with pytest.raises(ValueError):
         shard.rank_heads(BH, 3, 0)
 
