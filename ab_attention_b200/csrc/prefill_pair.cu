@@ -5,9 +5,10 @@
 // shift, ab_attention/flashinfer_backend.py:30-58,164-242).
 //
 // Adjacent query blocks share most of their sampled granules (the certain,
-// top-scored granules above all), so fetching the union once per pair moves
-// about two thirds of the bytes two separate CTAs would gather; the gather of
-// scattered 1 KB granules is what bounds the unpaired kernel.
+// top-scored granules above all: the union of two blocks is ~1.26x one block's
+// samples at the Wan shape), so fetching the union once per pair moves about two
+// thirds of the bytes two separate CTAs would gather, and each shared tile feeds
+// both blocks' products.
 //
 // Pair plan (pair_plan_kernel, one CTA per pair): the union as a list of
 // entries (16-bit slot of A | 16-bit slot of B << 16; 0xFFFF = not sampled by
@@ -578,7 +579,7 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_pair_kernel(const PairArg
         float m_used = -INFINITY;
         float l_sum = 0.f;
         bool ok = true;
-        // Lane j < 16 holds the weight of granule j of the current tile; the entry two
+        // Lane j holds the weight of granule j of the current tile; the entry two
         // tiles ahead and the weight one tile ahead are in flight.
         const int wl = lane & (kTileGranules - 1);
         uint32_t entry_next = kPadEntry;
