@@ -496,7 +496,7 @@ def main() -> None:
     if e2e is not None:
         line["e2e"] = e2e
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        line["cpu_baseline"] = cpu_sample(shape, rows_per_worker=96, workers=1)
+        line["cpu_baseline"] = cpu_sample(shape, rows_per_worker=192, workers=1)  # ~10 s of one core
         line["cpu_baseline"]["kind"] = "port"
     if rank == 0:
         print(json.dumps(line), flush=True)
