@@ -161,3 +161,23 @@ def test_out_of_range_id_reads_zeros_and_reports():
     lib.abx_device_status(None, 1, ctypes.byref(status))
     # the bad granule reads zeros in both kernels: same outputs up to rounding
     assert (o1.float() - o0.float()).abs().max().item() <= MAX_ERR
+
+
+@pytest.mark.parametrize("config,heads", [("wan14b", [0, 41]), ("hunyuan13b", [5])])
+def test_paired_matches_unpaired_at_full_size(config, heads):
+    """At the benchmark shapes (full-length rows, the production tile counts and
+    stage rings) the paired kernel computes the same attention as one block per
+    CTA, up to the order of the floating-point sums."""
+    from ab_attention_b200.synthetic import CONFIGS, make_inputs
+    shape = CONFIGS[config]
+    q, k, v, text = make_inputs(shape, "cuda", bh_slice=heads)
+    plan = build_plan(q, k, sample_pages=shape.sample_pages, seed=7)
+    rows = plan.descriptor.shape[0]
+    ids = plan.descriptor.reshape(rows, -1).contiguous()
+    logw = plan.log_weights.reshape(rows, -1).contiguous()
+    q3, k3, v3 = (x.reshape(-1, x.shape[2], 128) for x in (q, k, v))
+    tkv = None if text is None else tuple(t.reshape(-1, t.shape[2], 128) for t in text)
+    (o1, l1), (o0, l0) = _run_both(q3, k3, v3, ids, logw, text=tkv)
+    diff = (o1.float() - o0.float()).abs()
+    assert diff.max().item() <= MAX_ERR and diff.mean().item() <= MEAN_ERR / 4, (diff.max().item(), diff.mean().item())
+    assert (l1 - l0).abs().max().item() <= LSE_ERR
