@@ -265,8 +265,8 @@ constexpr int kThreads = (kVLoadWarp + kVGatherWarps) * 32;
 constexpr int kChunk = 16;
 constexpr int kChunks = kTileKeys / kChunk;
 constexpr int kLaunchRegs = 128;
-constexpr int kSoftmaxRegs = 192;  // a whole 128-column S row in registers
-constexpr int kProducerRegs = 64;
+constexpr int kSoftmaxRegs = 200;  // a whole 128-column S row in registers
+constexpr int kProducerRegs = 56;
 static_assert(kThreads == 512, "register split below assumes 16 warps");
 static_assert(kThreads * kLaunchRegs <= 65536, "launch register allocation exceeds the SM");
 static_assert(8 * 32 * kSoftmaxRegs + (kThreads - 8 * 32) * kProducerRegs <= kThreads * kLaunchRegs,
@@ -616,11 +616,14 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_pair_kernel(const PairArg
                 tc::tmem_reg_fence(r2);
                 tc::tmem_reg_fence(r3);
             }
-            // Row max of x = s * kappa + w (per granule: fma(max s, kappa, w)).
+            // Row max of x = s * kappa + w (per granule: fma(max s, kappa, w)); the
+            // granule weights stay in registers for the exponentials.
+            float wv[kTileGranules];
             float part_max[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
 #pragma unroll
             for (int gi = 0; gi < kTileGranules; ++gi) {
                 const float w = __shfl_sync(0xffffffffu, w_lane, gi);
+                wv[gi] = w;
                 const float smax = fmaxf(fmaxf(__uint_as_float(col(4 * gi)), __uint_as_float(col(4 * gi + 1))),
                                          fmaxf(__uint_as_float(col(4 * gi + 2)), __uint_as_float(col(4 * gi + 3))));
                 part_max[gi & 3] = fmaxf(part_max[gi & 3], fmaf(smax, args.kappa, w));
@@ -657,7 +660,7 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_pair_kernel(const PairArg
 #pragma unroll
                     for (int gi = 0; gi < kTileGranules / 4; ++gi) {
                         const int gg = quarter * (kTileGranules / 4) + gi;
-                        const float wm = __shfl_sync(0xffffffffu, w_lane, gg) - m_used;
+                        const float wm = wv[gg] - m_used;
                         const uint64_t wm2 = pack2(wm, wm);
 #pragma unroll
                         for (int h = 0; h < 2; ++h) {
