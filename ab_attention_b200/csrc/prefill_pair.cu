@@ -362,6 +362,13 @@ __device__ __forceinline__ int32_t code_row(const PairArgs& a, const RowBases& r
     return rb.text + (code - kTextCode) * kKv4;
 }
 
+// The largest of three floats in one instruction (sm_100 `max.f32` with three inputs).
+__device__ __forceinline__ float max3f(float a, float b, float c) {
+    float d;
+    asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+    return d;
+}
+
 // Logit shift of an entry for group g: its SIP weight, 0 for text, -inf when
 // the group's row did not sample it.
 __device__ __forceinline__ float entry_weight(const PairArgs& a, int64_t row_g, int g, uint32_t entry) {
@@ -624,7 +631,7 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_pair_kernel(const PairArg
             for (int gi = 0; gi < kTileGranules; ++gi) {
                 const float w = __shfl_sync(0xffffffffu, w_lane, gi);
                 wv[gi] = w;
-                const float smax = fmaxf(fmaxf(__uint_as_float(col(4 * gi)), __uint_as_float(col(4 * gi + 1))),
+                const float smax = max3f(__uint_as_float(col(4 * gi)), __uint_as_float(col(4 * gi + 1)),
                                          fmaxf(__uint_as_float(col(4 * gi + 2)), __uint_as_float(col(4 * gi + 3))));
                 part_max[gi & 3] = fmaxf(part_max[gi & 3], fmaf(smax, args.kappa, w));
             }
