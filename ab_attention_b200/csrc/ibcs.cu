@@ -645,7 +645,7 @@ __global__ __launch_bounds__(kMixThreads) void mix_kernel(const half* __restrict
     const int64_t row = blockIdx.x;
     if (threadIdx.x < kCentroids) {
         row_max[threadIdx.x] = lse_max[row * kCentroids + threadIdx.x];
-        row_den[threadIdx.x] = lse_den[row * kCentroids + threadIdx.x];
+        row_den[threadIdx.x] = mix_reciprocal(lse_den[row * kCentroids + threadIdx.x]);  // 1 / den
         row_weight[threadIdx.x] = populations[row * kCentroids + threadIdx.x];
     }
     __syncthreads();

@@ -17,12 +17,16 @@ __device__ __forceinline__ float mix_total_weight(const float* row_weight) {
     return total_weight;
 }
 
+// 1 / den of a centroid, taken once per row: the fast-math quotient x / den is
+// x times this reciprocal, so the scores keep their bits.
+__device__ __forceinline__ float mix_reciprocal(float den) { return 1.0f / den; }
+
 __device__ __forceinline__ float mix_score(const half (&value)[kCentroids], const float* row_max,
-                                           const float* row_den, const float* row_weight, float total_weight) {
+                                           const float* row_rden, const float* row_weight, float total_weight) {
     float score = 0.0f;
 #pragma unroll
     for (int c = 0; c < kCentroids; ++c) {
-        const float probability = exp2f(__half2float(value[c]) - row_max[c]) / row_den[c];
+        const float probability = exp2f(__half2float(value[c]) - row_max[c]) * row_rden[c];
         score += row_weight[c] * probability;
     }
     return score / total_weight;

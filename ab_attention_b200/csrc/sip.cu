@@ -59,7 +59,7 @@ struct MixedScores {
 #pragma unroll
         for (int c = 0; c < kCentroids; ++c) {
             mx[c] = lse_max[row * kCentroids + c];
-            den[c] = lse_den[row * kCentroids + c];
+            den[c] = mix_reciprocal(lse_den[row * kCentroids + c]);
             weight[c] = populations[row * kCentroids + c];
             value[c] = lse[(row * kCentroids + c) * ld + j];
         }
@@ -183,7 +183,7 @@ __global__ __launch_bounds__(kSipThreads) void sip_kernel(Source source, const f
         __shared__ float mix_max[kCentroids], mix_den[kCentroids], mix_weight[kCentroids];
         if (tid < kCentroids) {
             mix_max[tid] = source.lse_max[row * kCentroids + tid];
-            mix_den[tid] = source.lse_den[row * kCentroids + tid];
+            mix_den[tid] = mix_reciprocal(source.lse_den[row * kCentroids + tid]);  // 1 / den
             mix_weight[tid] = source.populations[row * kCentroids + tid];
         }
         __syncthreads();
