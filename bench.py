@@ -114,8 +114,8 @@ class ClockSampler:
 
 # DRAM bytes (read + write) of one paired prefill launch per head at the Wan shape,
 # from one ncu capture of the 2-head case (dram__bytes_read.sum + dram__bytes_write.sum
-# = 138.76 + 22.47 MB); a head's K/V stay L2-resident, so traffic scales with heads.
-PREFILL_DRAM_BYTES_PER_HEAD = (138.76e6 + 22.47e6) / 2
+# = 138.85 + 21.98 MB); a head's K/V stay L2-resident, so traffic scales with heads.
+PREFILL_DRAM_BYTES_PER_HEAD = (138.85e6 + 21.98e6) / 2
 
 
 def plan_bytes(bh: int, tokens: int, samples: int) -> float:
