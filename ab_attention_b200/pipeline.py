@@ -18,7 +18,7 @@ from .attention import apply_plan, build_plan
 
 
 @torch.no_grad()
-def ab_attention_host(q, k, v, *, sample_pages=64, seed=42, out=None, heads_per_chunk=8, device=None):
+def ab_attention_host(q, k, v, *, sample_pages=64, seed=42, out=None, heads_per_chunk=4, device=None):
     """``ab_attention`` for host tensors: q, k, v [B, H, N, 128] bf16 in host
     memory (pinned for overlap); returns the output in host memory (``out`` if
     given: [B, H, N, 128] bf16, pinned for overlap). Synchronizes before
