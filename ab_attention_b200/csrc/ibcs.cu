@@ -549,39 +549,59 @@ __global__ __launch_bounds__(kLseThreads, 3) void lse_kernel(const __grid_consta
         uint64_t dn[2] = {0, 0};
         const bool tma_out = args.vector_rows;
         const int swz = (lane >> 1) & 3;
-        bool ok = true;
-        for (int t = 0; t < tiles; ++t) {
-            const int b = t & 1;
-            if (!tc::mbar_wait_warp(bar(kLseBarTFull + b), (t >> 1) & 1, abort_flag, kLseWaitLimit,
-                                    tc::kLongWaitHintNs)) {
-                ok = false;
-                break;
-            }
+        // TMEM reads overlap the arithmetic: the high half of tile t is read while
+        // the low half is evaluated, and the low half of tile t + 1 while the high
+        // half of tile t is.
+        uint32_t lo[32], hi[32];
+        bool ok = tiles > 0 && tc::mbar_wait_warp(bar(kLseBarTFull), 0, abort_flag, kLseWaitLimit,
+                                                  tc::kLongWaitHintNs);
+        if (ok) {
             tc::fence_after_sync();
-            uint32_t lo[32], hi[32];
-            tc::tmem_ld32(lane_base + b * kLseTileKeys, lo);
-            tc::tmem_ld32(lane_base + b * kLseTileKeys + 32, hi);
+            tc::tmem_ld32(lane_base, lo);
             tc::tmem_wait_ld();
             tc::tmem_reg_fence(lo);
-            tc::tmem_reg_fence(hi);
-            tc::fence_before_sync();
-            tc::mbar_arrive(bar(kLseBarTEmpty + b));
+        }
+        for (int t = 0; ok && t < tiles; ++t) {
+            const int b = t & 1;
+            tc::tmem_ld32(lane_base + b * kLseTileKeys + 32, hi);
             const int j0 = t * kLseTileBlocks;
             const bool full = j0 + kLseTileBlocks <= args.fine_blocks;
+            const uint32_t buf = base + kLseOffOut + warp * kLseOutBufBytes;
+            const uint32_t row_addr = buf + lane * kLseStageRowBytes;
             if (tma_out) {
                 // This warp's staging buffer: the store issued from it for the
                 // previous tile must have finished reading it.
-                const uint32_t buf = base + kLseOffOut + warp * kLseOutBufBytes;
                 if (lane == 0) tc::bulk_wait_read<0>();
                 __syncwarp();
-                const uint32_t row_addr = buf + lane * kLseStageRowBytes;
-                if (full) {
+                if (full)
                     lse_tile<true, true>(lo, j0, args.fine_blocks, out, valid, row_addr, 0, swz, mx, dn);
-                    lse_tile<true, true>(hi, j0 + 16, args.fine_blocks, out, valid, row_addr, 2, swz, mx, dn);
-                } else {
+                else
                     lse_tile<false, true>(lo, j0, args.fine_blocks, out, valid, row_addr, 0, swz, mx, dn);
-                    lse_tile<false, true>(hi, j0 + 16, args.fine_blocks, out, valid, row_addr, 2, swz, mx, dn);
+            } else if (full) {
+                lse_tile<true, false>(lo, j0, args.fine_blocks, out, valid, 0, 0, 0, mx, dn);
+            } else {
+                lse_tile<false, false>(lo, j0, args.fine_blocks, out, valid, 0, 0, 0, mx, dn);
+            }
+            tc::tmem_wait_ld();
+            tc::tmem_reg_fence(hi);
+            tc::fence_before_sync();
+            tc::mbar_arrive(bar(kLseBarTEmpty + b));
+            const bool next = t + 1 < tiles;
+            if (next) {
+                const int nb = (t + 1) & 1;
+                if (tc::mbar_wait_warp(bar(kLseBarTFull + nb), ((t + 1) >> 1) & 1, abort_flag, kLseWaitLimit,
+                                       tc::kLongWaitHintNs)) {
+                    tc::fence_after_sync();
+                    tc::tmem_ld32(lane_base + nb * kLseTileKeys, lo);
+                } else {
+                    ok = false;
                 }
+            }
+            if (tma_out) {
+                if (full)
+                    lse_tile<true, true>(hi, j0 + 16, args.fine_blocks, out, valid, row_addr, 2, swz, mx, dn);
+                else
+                    lse_tile<false, true>(hi, j0 + 16, args.fine_blocks, out, valid, row_addr, 2, swz, mx, dn);
                 tc::fence_proxy_async_smem();
                 __syncwarp();
                 if (lane == 0) {
@@ -590,11 +610,13 @@ __global__ __launch_bounds__(kLseThreads, 3) void lse_kernel(const __grid_consta
                     tc::bulk_commit();
                 }
             } else if (full) {
-                lse_tile<true, false>(lo, j0, args.fine_blocks, out, valid, 0, 0, 0, mx, dn);
                 lse_tile<true, false>(hi, j0 + 16, args.fine_blocks, out, valid, 0, 0, 0, mx, dn);
             } else {
-                lse_tile<false, false>(lo, j0, args.fine_blocks, out, valid, 0, 0, 0, mx, dn);
                 lse_tile<false, false>(hi, j0 + 16, args.fine_blocks, out, valid, 0, 0, 0, mx, dn);
+            }
+            if (next && ok) {
+                tc::tmem_wait_ld();
+                tc::tmem_reg_fence(lo);
             }
         }
         // Every store issued above has completed before the CTA may exit.

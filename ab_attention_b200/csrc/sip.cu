@@ -116,6 +116,12 @@ __host__ __device__ constexpr size_t sip_prefix_region(int64_t population) {
 }
 
 constexpr int kLoadUnroll = 8;  // score loads in flight per thread
+// Rows ahead whose LSE rows a CTA prefetches into L2 (build_plan's form). Any
+// distance from 0 (the CTA's own row) to 32 measured the same at the Wan2.1
+// and HunyuanVideo shapes (SIP 8.0 -> 7.5 ms and 8.4 -> 7.6 ms per layer);
+// one or two waves of resident CTAs ahead (148 or 296 rows) measured slower
+// than no prefetch.
+constexpr int kSipPrefetchAhead = 8;
 constexpr int kMarkUnroll = 4;  // masses per thread per step of the marking sweep
 constexpr int kDrawGroup = 4;   // draws per thread searched in lockstep
 
@@ -128,7 +134,8 @@ template <class Source>
 __global__ __launch_bounds__(kSipThreads) void sip_kernel(Source source, const float* __restrict__ offsets,
                                                           int32_t* __restrict__ sampled,
                                                           float* __restrict__ weights, int population,
-                                                          int samples, int* device_error_word_ptr) {
+                                                          int samples, int prefetch_rows,
+                                                          int* device_error_word_ptr) {
     extern __shared__ __align__(16) double prefix[];
     Scratch& scratch = *reinterpret_cast<Scratch*>(prefix);
     __shared__ double scale;
@@ -181,6 +188,14 @@ __global__ __launch_bounds__(kSipThreads) void sip_kernel(Source source, const f
         // Mixture scores of this row, 8 consecutive blocks per step (one 16-byte
         // load per centroid; rows are padded to ld, so the last step stays inside).
         __shared__ float mix_max[kCentroids], mix_den[kCentroids], mix_weight[kCentroids];
+        // The LSE rows of the row `prefetch_rows` ahead in launch order go to L2
+        // by one bulk prefetch per centroid row (the whole 300 KB at once, where
+        // the fill below keeps 64 KB in flight), so that its CTA, starting a
+        // little later, fills mostly from L2.
+        const int64_t ahead = row + prefetch_rows;
+        if (prefetch_rows > 0 && ahead < gridDim.x && tid < kCentroids)
+            tc::prefetch_l2(source.lse + (ahead * kCentroids + tid) * source.ld,
+                            static_cast<uint32_t>(source.ld * sizeof(half)));
         if (tid < kCentroids) {
             mix_max[tid] = source.lse_max[row * kCentroids + tid];
             mix_den[tid] = mix_reciprocal(source.lse_den[row * kCentroids + tid]);  // 1 / den
@@ -501,9 +516,10 @@ static cudaError_t launch_sip_impl(const Source& source, const float* offsets, i
     cudaError_t err = cudaFuncSetAttribute(sip_kernel<Source>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                            static_cast<int>(smem));
     if (err != cudaSuccess) return err;
+    const int prefetch_rows = Source::kDense ? 0 : kSipPrefetchAhead;
     sip_kernel<Source><<<static_cast<unsigned>(rows), kSipThreads, smem, stream>>>(
         source, offsets, ids, log_weights, static_cast<int>(population), static_cast<int>(samples),
-        device_error_word());
+        prefetch_rows, device_error_word());
     return cudaGetLastError();
 }
 

@@ -291,6 +291,12 @@ __device__ __forceinline__ void bulk_load(uint32_t dst, const void* src, uint32_
                  : "memory");
 }
 
+// Hint: bring `bytes` (a multiple of 16, 16-byte aligned source) into L2. No
+// completion to wait for; the data is simply found in L2 by a later read.
+__device__ __forceinline__ void prefetch_l2(const void* src, uint32_t bytes) {
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;\n" ::"l"(src), "r"(bytes) : "memory");
+}
+
 // Store a box from shared memory through a 3-D tensor map (bulk async group);
 // elements outside the tensor are not written.
 __device__ __forceinline__ void tma_store_3d(const void* tmap, uint32_t src, int32_t x, int32_t y, int32_t z) {
