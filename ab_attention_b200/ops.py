@@ -28,6 +28,56 @@ def _as3(x: torch.Tensor) -> torch.Tensor:
     return x.contiguous()
 
 
+def _expect(t: torch.Tensor | None, name: str, shape, dtype: torch.dtype) -> None:
+    """`t` must be a contiguous tensor of exactly this shape and dtype: the C ABI
+    takes raw pointers, so a short or mistyped buffer would be read past its end."""
+    if t is None:
+        raise RuntimeError(f"{name} is required")
+    if t.dtype != dtype:
+        raise RuntimeError(f"{name} must be {dtype} (got {t.dtype})")
+    if tuple(t.shape) != tuple(shape):
+        raise RuntimeError(f"{name} must have shape {list(shape)} (got {list(t.shape)})")
+    if not t.is_contiguous():
+        raise RuntimeError(f"{name} must be contiguous")
+
+
+def _one_device(*tensors: torch.Tensor | None) -> None:
+    present = [t for t in tensors if t is not None]
+    _lib.require_cuda(*present)
+    if any(t.device != present[0].device for t in present):
+        raise RuntimeError("all tensors must be on one CUDA device")
+
+
+def _check_attention_inputs(q3, k3, v3, ids=None, logw=None, text_k=None, text_v=None, *, kv_tokens=None):
+    """q3 [BH,Nq,128] bf16; k3/v3 [BH,Nk,128] bf16 (Nk = Nq unless given; both None
+    when kv_tokens is 0); ids int32 and logw float32 [BH*ceil(Nq/128), samples];
+    text_k/text_v [BH,T,128] bf16 with T >= 1."""
+    if q3 is None or q3.ndim != 3:
+        raise RuntimeError("q must be [batch*heads, tokens, 128]")
+    bh, q_tokens, _ = q3.shape
+    _expect(q3, "q", (bh, q_tokens, HEAD_DIM), torch.bfloat16)
+    if not (kv_tokens == 0 and k3 is None and v3 is None):
+        nk = q_tokens if kv_tokens is None else kv_tokens
+        _expect(k3, "k", (bh, nk, HEAD_DIM), torch.bfloat16)
+        _expect(v3, "v", (bh, nk, HEAD_DIM), torch.bfloat16)
+    if (ids is None) != (logw is None):
+        raise RuntimeError("ids and log_weights are given together")
+    if ids is not None:
+        rows = bh * math.ceil(q_tokens / QUERY_BLOCK)
+        if ids.ndim != 2:
+            raise RuntimeError("ids must be [rows, samples]")
+        _expect(ids, "ids", (rows, ids.shape[1]), torch.int32)
+        _expect(logw, "log_weights", (rows, ids.shape[1]), torch.float32)
+    if (text_k is None) != (text_v is None):
+        raise RuntimeError("text_k and text_v are given together")
+    if text_k is not None:
+        if text_k.ndim != 3 or text_k.shape[1] == 0:
+            raise RuntimeError("text keys must be [batch*heads, T, 128] with T >= 1")
+        _expect(text_k, "text_k", (bh, text_k.shape[1], HEAD_DIM), torch.bfloat16)
+        _expect(text_v, "text_v", (bh, text_k.shape[1], HEAD_DIM), torch.bfloat16)
+    _one_device(q3, k3, v3, ids, logw, text_k, text_v)
+
+
 def _check_qk(q: torch.Tensor, k: torch.Tensor) -> None:
     _lib.require_cuda(q, k)
     if q.device != k.device:
@@ -83,14 +133,19 @@ def pool(k: torch.Tensor) -> torch.Tensor:
 
 def lse(scaled: torch.Tensor, pooled: torch.Tensor, q_blocks: int):
     """scaled centroids [BH*qb,8,128], pooled [BH,F,2,128] -> (lse fp16 [rows,8,F], max f32 [rows,8], den f32 [rows,8])."""
+    if pooled.ndim != 4:
+        raise RuntimeError("pooled must be [batch*heads, tokens/4, 2, 128]")
     bh, fine = pooled.shape[0], pooled.shape[1]
     rows = bh * q_blocks
+    _expect(pooled, "pooled", (bh, fine, 2, HEAD_DIM), torch.bfloat16)
+    _expect(scaled, "scaled centroids", (rows, CENTROIDS, HEAD_DIM), torch.bfloat16)
+    _one_device(scaled, pooled)
     out = torch.empty((rows, CENTROIDS, fine), dtype=torch.float16, device=pooled.device)
     mx = torch.empty((rows, CENTROIDS), dtype=torch.float32, device=pooled.device)
     den = torch.empty_like(mx)
     lib = _lib.load()
     with torch.cuda.device(pooled.device):
-        _lib.check(lib.abx_ibcs_lse(_lib.ptr(scaled.contiguous()), _lib.ptr(pooled.contiguous()), bh, q_blocks, fine,
+        _lib.check(lib.abx_ibcs_lse(_lib.ptr(scaled), _lib.ptr(pooled), bh, q_blocks, fine,
                                     _lib.ptr(out), _lib.ptr(mx), _lib.ptr(den), _lib.stream_of(pooled)),
                    "abx_ibcs_lse")
     return out, mx, den
@@ -98,13 +153,20 @@ def lse(scaled: torch.Tensor, pooled: torch.Tensor, q_blocks: int):
 
 def mix(lse_: torch.Tensor, populations: torch.Tensor, lse_max: torch.Tensor, lse_den: torch.Tensor):
     """Population-weighted mixture -> scores f32 [rows, F]."""
+    if lse_.ndim != 3:
+        raise RuntimeError("lse must be [rows, 8, F]")
     rows, _, fine = lse_.shape
+    _expect(lse_, "lse", (rows, CENTROIDS, fine), torch.float16)
+    pops = populations.to(torch.float32).contiguous()
+    _expect(pops, "populations", (rows, CENTROIDS), torch.float32)
+    _expect(lse_max, "lse_max", (rows, CENTROIDS), torch.float32)
+    _expect(lse_den, "lse_den", (rows, CENTROIDS), torch.float32)
+    _one_device(lse_, pops, lse_max, lse_den)
     out = torch.empty((rows, fine), dtype=torch.float32, device=lse_.device)
     lib = _lib.load()
-    pops = populations.to(torch.float32).contiguous()
     with torch.cuda.device(lse_.device):
-        _lib.check(lib.abx_ibcs_mix(_lib.ptr(lse_.contiguous()), _lib.ptr(pops), _lib.ptr(lse_max.contiguous()),
-                                    _lib.ptr(lse_den.contiguous()), rows, fine, _lib.ptr(out),
+        _lib.check(lib.abx_ibcs_mix(_lib.ptr(lse_), _lib.ptr(pops), _lib.ptr(lse_max),
+                                    _lib.ptr(lse_den), rows, fine, _lib.ptr(out),
                                     _lib.stream_of(lse_)), "abx_ibcs_mix")
     return out
 
@@ -151,7 +213,17 @@ def sip(scores: torch.Tensor, offsets: torch.Tensor, ids: torch.Tensor, logs: to
 def build_plan_into(q3: torch.Tensor, k3: torch.Tensor, offsets: torch.Tensor, ids: torch.Tensor,
                     logw: torch.Tensor, workspace: torch.Tensor) -> None:
     """Fused IBCS + SIP for contiguous [BH,S,128] q/k into [rows, samples] ids/logw."""
+    if q3.ndim != 3 or ids.ndim != 2:
+        raise RuntimeError("expected q/k [batch*heads, tokens, 128] and ids/log_weights [rows, samples]")
     bh, seq, _ = q3.shape
+    rows = bh * math.ceil(seq / QUERY_BLOCK)
+    _expect(q3, "q", (bh, seq, HEAD_DIM), torch.bfloat16)
+    _expect(k3, "k", (bh, seq, HEAD_DIM), torch.bfloat16)
+    _expect(offsets, "offsets", (rows,), torch.float32)
+    _expect(ids, "ids", (rows, ids.shape[1]), torch.int32)
+    _expect(logw, "log_weights", (rows, ids.shape[1]), torch.float32)
+    _expect(workspace, "workspace", (workspace.numel(),), torch.uint8)
+    _one_device(q3, k3, offsets, ids, logw, workspace)
     lib = _lib.load()
     with torch.cuda.device(q3.device):
         _lib.check(lib.abx_build_plan(_lib.ptr(q3), _lib.ptr(k3), bh, seq, _lib.ptr(offsets), ids.shape[-1],
@@ -166,6 +238,7 @@ def sparse_prefill(q3, k3, v3, ids, logw, *, text_k=None, text_v=None, return_ls
     of the union of their samples (abx_sparse_prefill_paired); False runs one
     query block per CTA (abx_sparse_prefill). Both compute the same attention.
     """
+    _check_attention_inputs(q3, k3, v3, ids, logw, text_k, text_v)
     bh, seq, _ = q3.shape
     samples = ids.shape[-1]
     o = torch.empty_like(q3)
@@ -194,6 +267,7 @@ def sparse_prefill(q3, k3, v3, ids, logw, *, text_k=None, text_v=None, return_ls
 
 def dense_prefill(q3, k3, v3, *, return_lse=False):
     """Dense attention through the same prefill kernel (the dense comparator)."""
+    _check_attention_inputs(q3, k3, v3)
     bh, seq, _ = q3.shape
     o = torch.empty_like(q3)
     lse_ = torch.empty((bh, seq), dtype=torch.float32, device=q3.device) if return_lse else None
@@ -208,8 +282,14 @@ def cross_prefill(q3, k3, v3, *, ids=None, logw=None, samples=0, text_k=None, te
     """q3 [BH,Nq,128] over `samples` granules of k3/v3 [BH,Nk,128] (the plan's ids
     with their log weights, or the first `samples` in order when ids is None)
     followed by every key of text_k/text_v [BH,T,128] (any T)."""
-    bh, q_tokens, _ = q3.shape
     kv_tokens = 0 if k3 is None else k3.shape[1]
+    if text_k is not None and text_v is not None and text_k.ndim == 3 and text_k.shape[1] == 0 \
+            and text_v.shape == text_k.shape:
+        text_k = text_v = None  # an empty prompt adds no keys
+    if ids is not None and ids.ndim == 2 and ids.shape[1] != samples:
+        raise RuntimeError(f"samples ({samples}) must equal the ids' column count ({ids.shape[1]})")
+    _check_attention_inputs(q3, k3, v3, ids, logw, text_k, text_v, kv_tokens=kv_tokens)
+    bh, q_tokens, _ = q3.shape
     o = torch.empty_like(q3)
     lse_ = torch.empty((bh, q_tokens), dtype=torch.float32, device=q3.device) if return_lse else None
     text_tokens = 0 if text_k is None else text_k.shape[1]

@@ -1,6 +1,7 @@
 """The C ABI library loads and exports every symbol include/abx.h declares;
 host-side argument validation answers without touching a GPU."""
 import ctypes
+import re
 
 import pytest
 
@@ -127,3 +128,45 @@ def test_paired_prefill_workspace_and_validation():
     assert lib.abx_sparse_prefill_paired(p, p, p, 1, 1024, p, None, 8, None, None, 0, p, None, p, 1 << 30, None) == 1
     assert lib.abx_sparse_prefill_paired(ctypes.c_void_p(18), p, p, 1, 1024, p, p, 8, None, None, 0, p, None, p,
                                          1 << 30, None) == 1
+
+
+def test_op_wrappers_check_buffers_before_passing_pointers():
+    """The tensor wrappers hand raw pointers to the C ABI, so every buffer's dtype,
+    exact shape and contiguity is checked first (a short ids or text tensor would
+    otherwise be read past its end on the device)."""
+    import torch
+
+    from ab_attention_b200 import _lib, ops
+
+    bf = torch.bfloat16
+    q = torch.zeros(2, 256, 128, dtype=bf)            # BH 2, 256 tokens -> 4 rows
+    ids = torch.zeros(4, 32, dtype=torch.int32)
+    logw = torch.zeros(4, 32)
+    bad = [
+        (lambda: ops.sparse_prefill(q, q, q, ids[:3], logw[:3]), "ids must have shape"),
+        (lambda: ops.sparse_prefill(q, q, q, ids, logw[:, :16]), "log_weights must have shape"),
+        (lambda: ops.sparse_prefill(q.half(), q, q, ids, logw), "q must be torch.bfloat16"),
+        (lambda: ops.sparse_prefill(q, q[:, :128], q, ids, logw), "k must have shape"),
+        (lambda: ops.sparse_prefill(q, q, q, ids, logw, text_k=torch.zeros(2, 8, 128, dtype=bf),
+                                    text_v=torch.zeros(2, 4, 128, dtype=bf)), "text_v must have shape"),
+        (lambda: ops.sparse_prefill(q, q, q, ids.t(), logw.t()), "ids must have shape"),
+        (lambda: ops.dense_prefill(q, q, q.transpose(1, 2).contiguous().transpose(1, 2)), "v must be contiguous"),
+        (lambda: ops.cross_prefill(q, q, q, ids=ids, logw=logw, samples=16), "samples (16) must equal"),
+        (lambda: ops.cross_prefill(q, None, None, samples=0, text_k=torch.zeros(1, 8, 128, dtype=bf),
+                                   text_v=torch.zeros(1, 8, 128, dtype=bf)), "text_k must have shape"),
+        (lambda: ops.lse(torch.zeros(7, 8, 128, dtype=bf), torch.zeros(2, 64, 2, 128, dtype=bf), 4),
+         "scaled centroids must have shape"),
+        (lambda: ops.mix(torch.zeros(4, 8, 64, dtype=torch.float16), torch.zeros(4, 8), torch.zeros(4, 8),
+                         torch.zeros(3, 8)), "lse_den must have shape"),
+        (lambda: ops.build_plan_into(q, q, torch.zeros(3), ids, logw, torch.zeros(16, dtype=torch.uint8)),
+         "offsets must have shape"),
+    ]
+    for call, message in bad:
+        with pytest.raises(RuntimeError, match=re.escape(message)):
+            call()
+    # well-formed host tensors get as far as the device check, and no further
+    with pytest.raises(_lib.AbxError, match="CUDA"):
+        ops.sparse_prefill(q, q, q, ids, logw)
+    with pytest.raises(_lib.AbxError, match="CUDA"):
+        ops.cross_prefill(q, None, None, samples=0, text_k=torch.zeros(2, 0, 128, dtype=bf),
+                          text_v=torch.zeros(2, 0, 128, dtype=bf))
