@@ -65,7 +65,7 @@ bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) ==
 // Workspace of the IBCS stages for (bh, seq).
 struct IbcsLayout {
     int64_t qb, rows, fine, ld;
-    size_t scaled, populations, pooled, lse, lse_max, lse_den, scores, total;
+    size_t scaled, populations, pooled, lse, lse_max, lse_den, total;
 };
 
 IbcsLayout ibcs_layout(int64_t bh, int64_t seq) {
@@ -87,8 +87,8 @@ IbcsLayout ibcs_layout(int64_t bh, int64_t seq) {
     off = align_up(off + static_cast<size_t>(l.rows) * abx::kCentroids * 4);
     l.lse_den = off;
     off = align_up(off + static_cast<size_t>(l.rows) * abx::kCentroids * 4);
-    l.scores = off;  // build_plan's block scores (abx_ibcs_scores writes the caller's array instead)
-    off = align_up(off + static_cast<size_t>(l.rows) * l.fine * 4);
+    // No block-score array: abx_build_plan's SIP evaluates the mixture from the
+    // LSE rows, and abx_ibcs_scores writes the caller's scores.
     l.total = off;
     return l;
 }
