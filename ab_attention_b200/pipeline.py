@@ -18,11 +18,14 @@ from .attention import apply_plan, build_plan
 
 
 @torch.no_grad()
-def ab_attention_host(q, k, v, *, sample_pages=64, seed=42, out=None, heads_per_chunk=4, device=None):
+def ab_attention_host(q, k, v, *, sample_pages=64, seed=42, out=None, heads_per_chunk=4, device=None,
+                      text_kv=None):
     """``ab_attention`` for host tensors: q, k, v [B, H, N, 128] bf16 in host
     memory (pinned for overlap); returns the output in host memory (``out`` if
-    given: [B, H, N, 128] bf16, pinned for overlap). Synchronizes before
-    returning."""
+    given: [B, H, N, 128] bf16, pinned for overlap). ``text_kv=(text_k, text_v)``
+    ([B, H, T, 128] bf16, host or device; moved to the device once) adds prompt
+    keys every query block includes with weight pi = 1, as ``apply_plan``'s
+    ``text_kv``. Synchronizes before returning."""
     if q.device.type != "cpu" or k.device.type != "cpu" or v.device.type != "cpu":
         raise ValueError("ab_attention_host takes host tensors")
     if q.ndim != 4 or q.shape != k.shape or q.shape != v.shape or q.dtype != torch.bfloat16 or q.shape[-1] != 128:
@@ -37,6 +40,11 @@ def ab_attention_host(q, k, v, *, sample_pages=64, seed=42, out=None, heads_per_
         raise ValueError("out must be a host tensor shaped like q")
     flat = [x.reshape(bh, tokens, dim) for x in (q, k, v)]
     out_flat = out.view(bh, tokens, dim)
+    if text_kv is not None:
+        text_k, text_v = text_kv
+        if text_k.shape != text_v.shape or text_k.ndim != 4 or text_k.shape[:2] != q.shape[:2] \
+                or text_k.shape[-1] != dim or text_k.dtype != q.dtype or text_v.dtype != q.dtype:
+            raise ValueError("text_kv must be two [B,H,T,128] bf16 tensors matching Q's batch and heads")
     chunk = max(1, min(heads_per_chunk, bh))
     starts = list(range(0, bh, chunk))
 
@@ -47,6 +55,9 @@ def ab_attention_host(q, k, v, *, sample_pages=64, seed=42, out=None, heads_per_
         copy_in.wait_stream(main)  # work the caller queued before this call comes first
         generator = torch.Generator(device=device).manual_seed(seed)
         offsets = torch.rand(bh * qb, device=device, generator=generator)
+        text = None
+        if text_kv is not None:
+            text = tuple(t.reshape(bh, -1, dim).to(device) for t in text_kv)
         # two device slots per input so chunk c + 1 lands while chunk c computes
         slots = [[torch.empty((chunk, tokens, dim), dtype=q.dtype, device=device) for _ in range(3)]
                  for _ in range(2)]
@@ -73,7 +84,8 @@ def ab_attention_host(q, k, v, *, sample_pages=64, seed=42, out=None, heads_per_
             main.wait_event(landed[s])
             qs, ks, vs = (x[:n].unsqueeze(0) for x in slots[s])
             plan = build_plan(qs, ks, sample_pages=sample_pages, offsets=offsets[a * qb:b * qb])
-            o = apply_plan(qs, ks, vs, plan)
+            block_text = None if text is None else tuple(t[a:b].unsqueeze(0) for t in text)
+            o = apply_plan(qs, ks, vs, plan, text_kv=block_text)
             freed[s].record(main)
             done = torch.cuda.Event()
             done.record(main)

@@ -119,3 +119,78 @@ def attention_sharded(q, k, v, offsets, out, *, world: int, chunks: int, sample_
         if work is not None:
             work.wait()
     return out
+
+
+def attention_sharded_host(q, k, v, offsets, out, host_out, *, world: int, chunks: int, sample_pages: int = 64,
+                           text_kv=None, group=None):
+    """`attention_sharded` for Q/K/V in host memory, with the copies overlapped.
+
+    q, k, v: pinned host [1, per, S, 128] bf16, the rank's heads in
+    `rank_heads(BH, world, rank, chunks)` order; offsets: their rows of
+    `layer_offsets` on the device; out: [BH, S, 128] bf16 on the device,
+    receives every rank's output; host_out: pinned host [1, per, S, 128],
+    receives this rank's heads. text_kv (optional): the rank's prompt keys and
+    values on the device, [1, per, T, 128] each.
+
+    Head block c + 1 is copied in on a side stream while block c is planned,
+    attended and all-gathered, and block c's own heads are copied out on a
+    third stream, so the layer costs about its host transfers rather than their
+    sum with the compute. The plan of each block is built from its rows of the
+    layer's offsets, so it is bit-identical to `attention_sharded`'s. Every
+    rank issues the same all-gathers in the same order. Returns when `out` and
+    host_out are complete on the current stream.
+    """
+    from .attention import apply_plan, build_plan
+
+    per, tokens, dim = q.shape[1], q.shape[2], q.shape[3]
+    if per % chunks:
+        raise ValueError(f"{per} local heads do not split into {chunks} blocks")
+    if q.device.type != "cpu" or k.device.type != "cpu" or v.device.type != "cpu" or host_out.device.type != "cpu":
+        raise ValueError("q, k, v and host_out must be host tensors")
+    if host_out.shape != q.shape or host_out.dtype != q.dtype:
+        raise ValueError("host_out must be shaped like q")
+    ch = per // chunks
+    qb = math.ceil(tokens / 128)
+    device = out.device
+    main = torch.cuda.current_stream(device)
+    copy_in = torch.cuda.Stream(device)
+    copy_out = torch.cuda.Stream(device)
+    copy_in.wait_stream(main)  # work the caller queued before this call comes first
+    # two device slots per input so block c + 1 lands while block c computes
+    slots = [[torch.empty((1, ch, tokens, dim), dtype=q.dtype, device=device) for _ in range(3)] for _ in range(2)]
+    landed = [torch.cuda.Event() for _ in range(2)]
+    freed = [torch.cuda.Event() for _ in range(2)]
+
+    def load(c):
+        s = c % 2
+        with torch.cuda.stream(copy_in):
+            if c >= 2:
+                copy_in.wait_event(freed[s])  # the slot's previous block has been consumed
+            for dst, src in zip(slots[s], (q, k, v)):
+                dst.copy_(src[:, c * ch:(c + 1) * ch], non_blocking=True)
+            landed[s].record(copy_in)
+
+    works = []
+    load(0)
+    for c in range(chunks):
+        if c + 1 < chunks:
+            load(c + 1)
+        s = c % 2
+        main.wait_event(landed[s])
+        qs, ks, vs = slots[s]
+        plan = build_plan(qs, ks, sample_pages=sample_pages, offsets=offsets[c * ch * qb:(c + 1) * ch * qb])
+        block_text = None if text_kv is None else tuple(t[:, c * ch:(c + 1) * ch] for t in text_kv)
+        o = apply_plan(qs, ks, vs, plan, text_kv=block_text)
+        freed[s].record(main)
+        works.append(gather_block(out, o.reshape(ch, tokens, dim), world, c, group=group, async_op=True))
+        done = torch.cuda.Event()
+        done.record(main)
+        with torch.cuda.stream(copy_out):
+            copy_out.wait_event(done)
+            host_out[:, c * ch:(c + 1) * ch].copy_(o, non_blocking=True)
+            o.record_stream(copy_out)
+    for work in works:
+        if work is not None:
+            work.wait()
+    main.wait_stream(copy_out)
+    return out

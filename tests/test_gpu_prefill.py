@@ -141,14 +141,48 @@ def test_torch_ops_and_paged_attention_match_python_api():
     assert torch.equal(ids2, ids) and torch.equal(logw2, logw)
 
 
-def test_host_pipeline_equals_device_path():
+@pytest.mark.parametrize("with_text", [False, True])
+def test_host_pipeline_equals_device_path(with_text):
     """ab_attention_host (chunked copy-in / compute / copy-out) gives the device
-    path's result bit for bit, including a ragged last chunk."""
-    from ab_attention_b200 import ab_attention, ab_attention_host
+    path's result bit for bit, including a ragged last chunk, with and without
+    prompt keys."""
+    from ab_attention_b200 import ab_attention_host
 
     q, k, v = (x.reshape(1, 5, -1, 128) for x in smooth_field(5, 2, 16, 32, seed=12, device="cuda"))
-    want = ab_attention(q, k, v, sample_pages=2, seed=7)
+    text = None
+    if with_text:
+        gen = torch.Generator(device="cuda").manual_seed(6)
+        text = tuple(torch.randn(1, 5, 37, 128, generator=gen, device="cuda").to(torch.bfloat16) for _ in range(2))
+    want = apply_plan(q, k, v, build_plan(q, k, sample_pages=2, seed=7), text_kv=text)
     hq, hk, hv = (x.cpu().pin_memory() for x in (q, k, v))
-    got = ab_attention_host(hq, hk, hv, sample_pages=2, seed=7, heads_per_chunk=2)
+    host_text = None if text is None else tuple(t.cpu() for t in text)
+    got = ab_attention_host(hq, hk, hv, sample_pages=2, seed=7, heads_per_chunk=2, text_kv=host_text)
     assert got.device.type == "cpu"
     assert torch.equal(got, want.cpu())
+
+
+@pytest.mark.parametrize("with_text", [False, True])
+def test_sharded_host_pipeline_equals_device_path(with_text):
+    """attention_sharded_host (block copy-in / plan + prefill + gather / copy-out on
+    three streams), run as one rank, gives the device path's result bit for bit
+    in both the gathered device output and the host output."""
+    from ab_attention_b200 import shard
+
+    heads, chunks = 4, 2
+    q, k, v = (x.reshape(1, heads, -1, 128) for x in smooth_field(heads, 2, 16, 32, seed=13, device="cuda"))
+    tokens = q.shape[2]
+    text = None
+    if with_text:
+        gen = torch.Generator(device="cuda").manual_seed(5)
+        text = tuple(torch.randn(1, heads, 37, 128, generator=gen, device="cuda").to(torch.bfloat16)
+                     for _ in range(2))
+    offsets = shard.layer_offsets(heads, tokens, seed=3, device="cuda")
+    want = apply_plan(q, k, v, build_plan(q, k, sample_pages=2, offsets=offsets), text_kv=text)
+    hq, hk, hv = (x.cpu().pin_memory() for x in (q, k, v))
+    host_out = torch.empty(q.shape, dtype=q.dtype).pin_memory()
+    out = torch.empty((heads, tokens, 128), dtype=torch.bfloat16, device="cuda")
+    shard.attention_sharded_host(hq, hk, hv, offsets, out, host_out, world=1, chunks=chunks, sample_pages=2,
+                                 text_kv=text)
+    torch.cuda.synchronize()
+    assert torch.equal(out, want[0])
+    assert torch.equal(host_out, want.cpu())
