@@ -390,24 +390,17 @@ def main() -> None:
         d2h = hout.numel() * hout.element_size()
 
         def e2e_step():
-            dq, dk, dv = (x.to(device, non_blocking=True) for x in (hq, hk, hv))
-            o = step(None, dq, dk, dv)
-            if world > 1:
-                # this rank's heads of the gathered layer output, block by block
-                ch = per // chunks
-                for c in range(chunks):
-                    first = (c * world + rank) * ch
-                    hout[0, c * ch:(c + 1) * ch].copy_(o[first:first + ch], non_blocking=True)
-            else:
-                hout.copy_(o, non_blocking=True)
-            return o
+            # head blocks stream through: block c + 1 copied in while block c is
+            # planned, attended and all-gathered, block c's own heads copied out
+            return shard.attention_sharded_host(hq, hk, hv, offsets, gathered, hout, world=world, chunks=chunks,
+                                                sample_pages=shape.sample_pages, text_kv=text)
 
         if world == 1:
             # the public host-buffer entry point: copy-in, compute and copy-out of
-            # head chunks overlap on three streams
+            # head chunks overlap on three streams (prompt keys stay on the device)
             def e2e_step():  # noqa: F811
                 return abx.ab_attention_host(hq, hk, hv, sample_pages=shape.sample_pages, seed=shape.seed,
-                                             out=hout.view(q.shape), device=device)
+                                             out=hout.view(q.shape), device=device, text_kv=text)
 
         e2e_step()
         torch.cuda.synchronize()
