@@ -229,11 +229,10 @@ static int run_ibcs_front(const void* q, const void* k, int64_t bh, int64_t seq,
     auto* lse = reinterpret_cast<half*>(ws + l.lse);
     auto* mx = reinterpret_cast<float*>(ws + l.lse_max);
     auto* den = reinterpret_cast<float*>(ws + l.lse_den);
+    // clustering and key pooling in one launch
     if (int st = check_cuda(abx::launch_cluster(static_cast<const abx::bf16*>(q), bh, seq, nullptr, scaled,
-                                                pops, nullptr, stream), "cluster launch"))
-        return st;
-    if (int st = check_cuda(abx::launch_pool(static_cast<const abx::bf16*>(k), bh, seq, pooled, stream),
-                            "pool launch"))
+                                                pops, nullptr, stream, static_cast<const abx::bf16*>(k), pooled),
+                            "cluster launch"))
         return st;
     return check_cuda(abx::launch_lse(scaled, pooled, bh, l.qb, l.fine, l.ld, lse, mx, den, stream), "lse launch");
 }

@@ -116,10 +116,38 @@ __device__ __forceinline__ int argmax128(float value, int index, float* red_val,
     return best_index;
 }
 
+// The pooled representatives of one KV4 block's 8-dim chunk (pool_keys_kernel,
+// csrc/ibcs.cu:244-266): p_t = bf16_rn(0.5f * (k_{2t} + k_{2t+1})), t = 0, 1.
+__device__ __forceinline__ void pool_chunk(const bf16* __restrict__ k, bf16* __restrict__ pooled, int64_t block,
+                                           int chunk) {
+    const uint4* src = reinterpret_cast<const uint4*>(k + block * kKv4 * kHeadDim) + chunk;
+    uint4 rows[4];
+#pragma unroll
+    for (int r = 0; r < 4; ++r) rows[r] = __ldg(src + r * 16);
+    uint4 out[2];
+#pragma unroll
+    for (int rep = 0; rep < 2; ++rep) {
+        const bf16* a = reinterpret_cast<const bf16*>(&rows[2 * rep]);
+        const bf16* b = reinterpret_cast<const bf16*>(&rows[2 * rep + 1]);
+        bf16* o = reinterpret_cast<bf16*>(&out[rep]);
+#pragma unroll
+        for (int e = 0; e < 8; ++e)
+            o[e] = __float2bfloat16_rn(0.5f * (__bfloat162float(a[e]) + __bfloat162float(b[e])));
+    }
+    uint4* dst = reinterpret_cast<uint4*>(pooled + block * kReps * kHeadDim) + chunk;
+    dst[0] = out[0];
+    dst[16] = out[1];
+}
+
+// k / pooled (both or neither): the CTA of query block r also pools the KV4
+// blocks of the same 128 tokens (blocks 32r .. 32r + 31 of the head), so the
+// key pooling rides on the clustering's latency-bound pass instead of a launch
+// of its own.
 __global__ __launch_bounds__(128) void cluster_kernel(
     const bf16* __restrict__ q, int64_t seq, int64_t qb, bf16* __restrict__ centroids,
     bf16* __restrict__ scaled, float* __restrict__ populations,
-    int32_t* __restrict__ assignments, float kappa) {
+    int32_t* __restrict__ assignments, float kappa, const bf16* __restrict__ k,
+    bf16* __restrict__ pooled) {
     __shared__ uint4 tile[128 * 16];
     __shared__ __align__(16) float center[kHeadDim];
     __shared__ int members[kQueryBlock];
@@ -142,6 +170,12 @@ __global__ __launch_bounds__(128) void cluster_kernel(
         uint4 v = make_uint4(0u, 0u, 0u, 0u);
         if (i < n) v = src[i * 16 + c];
         tile[chunk_slot(i, c)] = v;
+    }
+    if (pooled != nullptr) {
+        // n is a multiple of 4 (seq % 4 == 0, token0 % 128 == 0): whole KV4 blocks
+        const int64_t block0 = head * (seq / kKv4) + token0 / kKv4;
+        const int items = (n / kKv4) * 16;
+        for (int it = tid; it < items; it += 128) pool_chunk(k, pooled, block0 + (it >> 4), it & 15);
     }
     __syncthreads();
 
@@ -228,25 +262,7 @@ __global__ __launch_bounds__(256) void pool_kernel(const bf16* __restrict__ k, i
                                                    bf16* __restrict__ pooled) {
     const int64_t idx = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
     if (idx >= chunks) return;
-    const int64_t block = idx >> 4;
-    const int chunk = static_cast<int>(idx & 15);
-    const uint4* src = reinterpret_cast<const uint4*>(k + block * kKv4 * kHeadDim) + chunk;
-    uint4 rows[4];
-#pragma unroll
-    for (int r = 0; r < 4; ++r) rows[r] = __ldg(src + r * 16);
-    uint4 out[2];
-#pragma unroll
-    for (int rep = 0; rep < 2; ++rep) {
-        const bf16* a = reinterpret_cast<const bf16*>(&rows[2 * rep]);
-        const bf16* b = reinterpret_cast<const bf16*>(&rows[2 * rep + 1]);
-        bf16* o = reinterpret_cast<bf16*>(&out[rep]);
-#pragma unroll
-        for (int e = 0; e < 8; ++e)
-            o[e] = __float2bfloat16_rn(0.5f * (__bfloat162float(a[e]) + __bfloat162float(b[e])));
-    }
-    uint4* dst = reinterpret_cast<uint4*>(pooled + block * kReps * kHeadDim) + chunk;
-    dst[0] = out[0];
-    dst[16] = out[1];
+    pool_chunk(k, pooled, idx >> 4, static_cast<int>(idx & 15));
 }
 
 // ---------------------------------------------------------------------------
@@ -713,11 +729,13 @@ __global__ __launch_bounds__(kMixThreads) void mix_kernel(const half* __restrict
 // ---------------------------------------------------------------------------
 
 cudaError_t launch_cluster(const bf16* q, int64_t bh, int64_t seq, bf16* centroids, bf16* scaled,
-                           float* populations, int32_t* assignments, cudaStream_t stream) {
+                           float* populations, int32_t* assignments, cudaStream_t stream, const bf16* k,
+                           bf16* pooled) {
+    if ((k == nullptr) != (pooled == nullptr)) return cudaErrorInvalidValue;
     const int64_t qb = ceil_div(seq, kQueryBlock);
     const int64_t rows = bh * qb;
     cluster_kernel<<<static_cast<unsigned>(rows), 128, 0, stream>>>(
-        q, seq, qb, centroids, scaled, populations, assignments, qk_scale_log2());
+        q, seq, qb, centroids, scaled, populations, assignments, qk_scale_log2(), k, pooled);
     return cudaGetLastError();
 }
 

@@ -6,8 +6,11 @@
 
 namespace abx {
 
+// With k and pooled (both or neither), the clustering launch also writes the
+// pooled key representatives (what launch_pool writes).
 cudaError_t launch_cluster(const bf16* q, int64_t bh, int64_t seq, bf16* centroids, bf16* scaled,
-                           float* populations, int32_t* assignments, cudaStream_t stream);
+                           float* populations, int32_t* assignments, cudaStream_t stream,
+                           const bf16* k = nullptr, bf16* pooled = nullptr);
 cudaError_t launch_pool(const bf16* k, int64_t bh, int64_t seq, bf16* pooled, cudaStream_t stream);
 size_t lse_smem_bytes();
 cudaError_t launch_lse(const bf16* scaled, const bf16* pooled, int64_t bh, int64_t qb,

@@ -473,7 +473,7 @@ def main() -> None:
                      "traffic": (PREFILL_DRAM_BYTES_PER_HEAD * per
                                  if shape.name.split("[")[0] == "wan14b" and shape.sample_pages == 64 else None),
                      "peak_source": peaks["source"] + " sustained bf16"},
-        "plan_roofline": {"kernels": "cluster+pool+lse+sip (mixture evaluated inside sip)", "bound": "hbm",
+        "plan_roofline": {"kernels": "cluster (with the key pooling) + lse + sip (mixture evaluated inside sip)", "bound": "hbm",
                           "achieved": plan_bytes(per, tokens, shape.sample_pages * 32) / (plan_ms * 1e-3) / 1e9,
                           "peak": peaks["hbm_gbs"], "unit": "GB/s",
                           "frac": plan_bytes(per, tokens, shape.sample_pages * 32) / (plan_ms * 1e-3) / 1e9
@@ -482,7 +482,7 @@ def main() -> None:
                                   "fast-math exp2/log2/division work and the double-precision SIP sums"},
         # cluster, pool, lse, sip + a pair plan and a prefill per head block per step
         # (NCCL's kernels not counted)
-        "gpu_launches": (4 + 2 * chunks) * args.steps,
+        "gpu_launches": (3 + 2 * chunks) * args.steps,
         "clocks": clocks.summary(),
         **dense,
     }
