@@ -3,6 +3,8 @@
 // Validates every argument on the host, lays out the caller-owned workspace,
 // and launches the kernels on the caller's stream. No allocation, no host
 // synchronisation (except abx_device_status, which reads the error word).
+#include <cuda.h>
+
 #include <cstdarg>
 #include <cstdio>
 #include <cstring>
@@ -297,25 +299,67 @@ namespace {
 constexpr size_t kStaticScratchBytes = size_t(256) << 20;
 static __device__ __align__(256) unsigned char g_static_scratch[kStaticScratchBytes];
 
-std::mutex g_static_scratch_mutex;
-constexpr int kMaxDevices = 64;
-void* g_static_scratch_ptr[kMaxDevices] = {};
+// Driver calls reached through the runtime's entry-point table (no libcuda link).
+using PfnCtxGetCurrent = CUresult (*)(CUcontext*);
+using PfnCtxGetId = CUresult (*)(CUcontext, unsigned long long*);
 
-// Device address of g_static_scratch on the current device. In host code the
-// array's name is only a host-side stand-in, so the address is looked up once
-// per device with cudaGetSymbolAddress (with that device current) and cached.
+template <class Fn>
+Fn driver_entry(const char* name) {
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult status;
+    if (cudaGetDriverEntryPoint(name, &ptr, cudaEnableDefault, &status) != cudaSuccess ||
+        status != cudaDriverEntryPointSuccess)
+        return nullptr;
+    return reinterpret_cast<Fn>(ptr);
+}
+
+// The array's device address per CUDA context, keyed by the context's unique
+// id (cuCtxGetId never reuses an id within a process). A host that creates its
+// own context on a device, or that resets the device, gets a fresh lookup
+// instead of an address that belongs to another or a destroyed context.
+struct ScratchSlot {
+    unsigned long long context_id;
+    void* ptr;
+};
+constexpr int kScratchSlots = 64;
+std::mutex g_static_scratch_mutex;
+ScratchSlot g_static_scratch_slots[kScratchSlots] = {};
+int g_static_scratch_next = 0;
+
+// Device address of g_static_scratch in the calling thread's current context.
+// In host code the array's name is only a host-side stand-in, so the address
+// is looked up with cudaGetSymbolAddress (with that device current) once per
+// context and cached.
 int static_scratch(void** out) {
-    int device = -1;
-    if (int st = check_cuda(cudaGetDevice(&device), "cudaGetDevice")) return st;
-    if (device < 0 || device >= kMaxDevices) return fail(ABX_ERR_UNSUPPORTED, "device ordinal %d out of range", device);
-    std::lock_guard<std::mutex> lock(g_static_scratch_mutex);
-    if (g_static_scratch_ptr[device] == nullptr) {
+    static const PfnCtxGetCurrent ctx_get_current = driver_entry<PfnCtxGetCurrent>("cuCtxGetCurrent");
+    static const PfnCtxGetId ctx_get_id = driver_entry<PfnCtxGetId>("cuCtxGetId");
+    if (ctx_get_current == nullptr || ctx_get_id == nullptr)
+        return fail(ABX_ERR_CUDA, "cuCtxGetCurrent / cuCtxGetId unavailable in this driver");
+    CUcontext ctx = nullptr;
+    if (ctx_get_current(&ctx) != CUDA_SUCCESS || ctx == nullptr) {
+        // No context is bound to this thread yet: the symbol lookup initialises
+        // the current device's primary context and makes it current.
         void* ptr = nullptr;
         if (int st = check_cuda(cudaGetSymbolAddress(&ptr, g_static_scratch), "cudaGetSymbolAddress(static scratch)"))
             return st;
-        g_static_scratch_ptr[device] = ptr;
+        if (ctx_get_current(&ctx) != CUDA_SUCCESS || ctx == nullptr)
+            return fail(ABX_ERR_CUDA, "no current CUDA context after the symbol lookup");
     }
-    *out = g_static_scratch_ptr[device];
+    unsigned long long id = 0;
+    if (ctx_get_id(ctx, &id) != CUDA_SUCCESS) return fail(ABX_ERR_CUDA, "cuCtxGetId failed");
+    std::lock_guard<std::mutex> lock(g_static_scratch_mutex);
+    for (const ScratchSlot& slot : g_static_scratch_slots) {
+        if (slot.ptr != nullptr && slot.context_id == id) {
+            *out = slot.ptr;
+            return ABX_OK;
+        }
+    }
+    void* ptr = nullptr;
+    if (int st = check_cuda(cudaGetSymbolAddress(&ptr, g_static_scratch), "cudaGetSymbolAddress(static scratch)"))
+        return st;
+    g_static_scratch_slots[g_static_scratch_next] = ScratchSlot{id, ptr};
+    g_static_scratch_next = (g_static_scratch_next + 1) % kScratchSlots;
+    *out = ptr;
     return ABX_OK;
 }
 
@@ -392,6 +436,8 @@ int abx_sparse_prefill_paired(const void* q, const void* k, const void* v, int64
                               const int32_t* ids, const float* log_weights, int64_t samples, const void* text_k,
                               const void* text_v, int64_t text_tokens, void* o, float* lse, void* workspace,
                               size_t workspace_bytes, abx_stream_t stream) {
+    if (samples < 0 || text_tokens < 0)
+        return fail(ABX_ERR_INVALID_ARGUMENT, "negative sample or text token count");
     if (!abx::pair_supported(seq, samples, text_tokens) || ids == nullptr)
         return abx_sparse_prefill(q, k, v, bh, seq, ids, log_weights, samples, text_k, text_v, text_tokens, o, lse,
                                   stream);

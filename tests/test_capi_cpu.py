@@ -128,6 +128,9 @@ def test_paired_prefill_workspace_and_validation():
     assert lib.abx_sparse_prefill_paired(p, p, p, 1, 1024, p, None, 8, None, None, 0, p, None, p, 1 << 30, None) == 1
     assert lib.abx_sparse_prefill_paired(ctypes.c_void_p(18), p, p, 1, 1024, p, p, 8, None, None, 0, p, None, p,
                                          1 << 30, None) == 1
+    # negative counts are refused before the pairing decision, as the unpaired entry point does
+    assert lib.abx_sparse_prefill_paired(p, p, p, 1, 1024, p, p, 8, p, p, -4, p, None, p, 1 << 30, None) == 1
+    assert lib.abx_sparse_prefill_paired(p, p, p, 1, 1024, p, p, -8, None, None, 0, p, None, p, 1 << 30, None) == 1
 
 
 def test_op_wrappers_check_buffers_before_passing_pointers():

@@ -20,8 +20,6 @@ import torch
 from ab_attention_b200 import _lib, ops
 from ab_attention_b200.synthetic import smooth_field
 
-pytestmark = pytest.mark.gpu
-
 
 def _plan_with_workspace(lib, q, k, offsets, samples):
     bh, seq, _ = q.shape
@@ -44,7 +42,12 @@ def _plan_static(lib, q, k, offsets, samples):
     return ids, logw
 
 
-@pytest.mark.parametrize("grid,bh,samples", [((2, 16, 64), 3, 96), ((21, 45, 80), 2, 2048)])
+@pytest.mark.gpu
+@pytest.mark.parametrize("grid,bh,samples", [
+    ((2, 16, 64), 3, 96),      # every head in one pass
+    ((21, 45, 80), 2, 2048),   # Wan shape: one head per pass (about 190 MB of scratch each)
+    ((4, 64, 64), 30, 512),    # 16,384 tokens, ~10.7 MB per head: 24 heads, then a ragged pass of 6
+])
 def test_static_scratch_matches_workspace_entry_point(grid, bh, samples):
     lib = _lib.load()
     torch.cuda.set_device(0)
@@ -61,6 +64,7 @@ def test_static_scratch_matches_workspace_entry_point(grid, bh, samples):
 
 
 def test_static_scratch_rejects_inputs_beyond_its_size():
+    """Runs without a GPU: the size check answers before any CUDA call."""
     lib = _lib.load()
     assert lib.abx_static_scratch_bytes() == 256 << 20
     p = ctypes.c_void_p(256)
