@@ -38,6 +38,9 @@ _SIGNATURES = {
     "abx_prefill_workspace_size": ([_i64, _i64, _i64, _i64, ctypes.POINTER(ctypes.c_size_t)], ctypes.c_int),
     "abx_sparse_prefill_paired": ([_p, _p, _p, _i64, _i64, _p, _p, _i64, _p, _p, _i64, _p, _p, _p, ctypes.c_size_t,
                                    _p], ctypes.c_int),
+    "abx_pair_plan": ([_p, _i64, _i64, _i64, _i64, _p, ctypes.c_size_t, _p], ctypes.c_int),
+    "abx_sparse_prefill_paired_planned": ([_p, _p, _p, _i64, _i64, _p, _p, _i64, _p, _p, _i64, _p, _p, _p,
+                                           ctypes.c_size_t, _p], ctypes.c_int),
     "abx_dense_prefill": ([_p, _p, _p, _i64, _i64, _p, _p, _p], ctypes.c_int),
     "abx_cross_prefill": ([_p, _i64, _p, _p, _i64, _i64, _p, _p, _i64, _p, _p, _i64, _p, _p, _p], ctypes.c_int),
 }

@@ -432,6 +432,34 @@ int abx_prefill_workspace_size(int64_t bh, int64_t seq, int64_t samples, int64_t
     return ABX_OK;
 }
 
+}  // extern "C"
+
+namespace {
+
+// Arguments of the paired prefill once the shape is known to pair.
+int check_paired(const void* q, const void* k, const void* v, int64_t bh, int64_t seq, const int32_t* ids,
+                 const float* log_weights, int64_t samples, const void* text_k, const void* text_v,
+                 int64_t text_tokens, const void* o, const void* workspace, size_t workspace_bytes) {
+    if (int st = check_qk_shape(bh, seq)) return st;
+    if (!q || !k || !v || !o) return fail(ABX_ERR_INVALID_ARGUMENT, "q, k, v and o must be non-null");
+    if (!aligned16(q) || !aligned16(k) || !aligned16(v) || !aligned16(o))
+        return fail(ABX_ERR_INVALID_ARGUMENT, "q, k, v and o must be 16-byte aligned");
+    if (samples > seq / abx::kKv4)
+        return fail(ABX_ERR_INVALID_ARGUMENT, "samples must be in [0, seq/4] (got %lld)", (long long)samples);
+    if (ids == nullptr || log_weights == nullptr)
+        return fail(ABX_ERR_INVALID_ARGUMENT, "ids and log_weights must be non-null");
+    if (text_tokens > 0 && (!text_k || !text_v || !aligned16(text_k) || !aligned16(text_v)))
+        return fail(ABX_ERR_INVALID_ARGUMENT, "text_k/text_v must be non-null and 16-byte aligned");
+    if (workspace == nullptr || workspace_bytes < abx::pair_workspace_bytes(bh, seq, samples, text_tokens))
+        return fail(ABX_ERR_WORKSPACE, "workspace too small (%zu bytes, need %zu)", workspace_bytes,
+                    abx::pair_workspace_bytes(bh, seq, samples, text_tokens));
+    return ABX_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
 int abx_sparse_prefill_paired(const void* q, const void* k, const void* v, int64_t bh, int64_t seq,
                               const int32_t* ids, const float* log_weights, int64_t samples, const void* text_k,
                               const void* text_v, int64_t text_tokens, void* o, float* lse, void* workspace,
@@ -441,19 +469,43 @@ int abx_sparse_prefill_paired(const void* q, const void* k, const void* v, int64
     if (!abx::pair_supported(seq, samples, text_tokens) || ids == nullptr)
         return abx_sparse_prefill(q, k, v, bh, seq, ids, log_weights, samples, text_k, text_v, text_tokens, o, lse,
                                   stream);
+    if (int st = check_paired(q, k, v, bh, seq, ids, log_weights, samples, text_k, text_v, text_tokens, o, workspace,
+                              workspace_bytes))
+        return st;
+    return check_cuda(abx::launch_prefill_pair(static_cast<const abx::bf16*>(q), static_cast<const abx::bf16*>(k),
+                                               static_cast<const abx::bf16*>(v), bh, seq, ids, log_weights, samples,
+                                               static_cast<const abx::bf16*>(text_k),
+                                               static_cast<const abx::bf16*>(text_v), text_tokens,
+                                               static_cast<abx::bf16*>(o), lse, workspace, workspace_bytes, stream),
+                      "paired prefill launch");
+}
+
+int abx_pair_plan(const int32_t* ids, int64_t bh, int64_t seq, int64_t samples, int64_t text_tokens, void* workspace,
+                  size_t workspace_bytes, abx_stream_t stream) {
     if (int st = check_qk_shape(bh, seq)) return st;
-    if (!q || !k || !v || !o) return fail(ABX_ERR_INVALID_ARGUMENT, "q, k, v and o must be non-null");
-    if (!aligned16(q) || !aligned16(k) || !aligned16(v) || !aligned16(o))
-        return fail(ABX_ERR_INVALID_ARGUMENT, "q, k, v and o must be 16-byte aligned");
-    if (samples > seq / abx::kKv4)
-        return fail(ABX_ERR_INVALID_ARGUMENT, "samples must be in [0, seq/4] (got %lld)", (long long)samples);
-    if (log_weights == nullptr) return fail(ABX_ERR_INVALID_ARGUMENT, "ids and log_weights must be non-null");
-    if (text_tokens > 0 && (!text_k || !text_v || !aligned16(text_k) || !aligned16(text_v)))
-        return fail(ABX_ERR_INVALID_ARGUMENT, "text_k/text_v must be non-null and 16-byte aligned");
+    if (samples < 0 || text_tokens < 0) return fail(ABX_ERR_INVALID_ARGUMENT, "negative sample or text token count");
+    if (!abx::pair_supported(seq, samples, text_tokens))
+        return fail(ABX_ERR_UNSUPPORTED, "this shape cannot be paired (abx_prefill_workspace_size reports 0)");
+    if (ids == nullptr) return fail(ABX_ERR_INVALID_ARGUMENT, "ids must be non-null");
     if (workspace == nullptr || workspace_bytes < abx::pair_workspace_bytes(bh, seq, samples, text_tokens))
         return fail(ABX_ERR_WORKSPACE, "workspace too small (%zu bytes, need %zu)", workspace_bytes,
                     abx::pair_workspace_bytes(bh, seq, samples, text_tokens));
-    return check_cuda(abx::launch_prefill_pair(static_cast<const abx::bf16*>(q), static_cast<const abx::bf16*>(k),
+    return check_cuda(abx::launch_pair_plan(ids, bh, seq, samples, text_tokens, workspace, workspace_bytes, stream),
+                      "pair plan launch");
+}
+
+int abx_sparse_prefill_paired_planned(const void* q, const void* k, const void* v, int64_t bh, int64_t seq,
+                                      const int32_t* ids, const float* log_weights, int64_t samples,
+                                      const void* text_k, const void* text_v, int64_t text_tokens, void* o,
+                                      float* lse, void* workspace, size_t workspace_bytes, abx_stream_t stream) {
+    if (samples < 0 || text_tokens < 0)
+        return fail(ABX_ERR_INVALID_ARGUMENT, "negative sample or text token count");
+    if (!abx::pair_supported(seq, samples, text_tokens))
+        return fail(ABX_ERR_UNSUPPORTED, "this shape cannot be paired (abx_prefill_workspace_size reports 0)");
+    if (int st = check_paired(q, k, v, bh, seq, ids, log_weights, samples, text_k, text_v, text_tokens, o, workspace,
+                              workspace_bytes))
+        return st;
+    return check_cuda(abx::launch_pair_prefill(static_cast<const abx::bf16*>(q), static_cast<const abx::bf16*>(k),
                                                static_cast<const abx::bf16*>(v), bh, seq, ids, log_weights, samples,
                                                static_cast<const abx::bf16*>(text_k),
                                                static_cast<const abx::bf16*>(text_v), text_tokens,

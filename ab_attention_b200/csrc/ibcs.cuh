@@ -40,6 +40,15 @@ cudaError_t launch_prefill(const bf16* q, int64_t q_tokens, const bf16* k, const
 // their samples); pair_supported() says whether a shape can take it.
 bool pair_supported(int64_t seq, int64_t samples, int64_t text_tokens);
 size_t pair_workspace_bytes(int64_t bh, int64_t seq, int64_t samples, int64_t text_tokens);
+// The two launches of launch_prefill_pair: the union lists of each pair (written
+// into the workspace), then the prefill that reads them. A plan reused across
+// calls needs its union lists built once.
+cudaError_t launch_pair_plan(const int32_t* ids, int64_t bh, int64_t seq, int64_t samples, int64_t text_tokens,
+                             void* workspace, size_t workspace_bytes, cudaStream_t stream);
+cudaError_t launch_pair_prefill(const bf16* q, const bf16* k, const bf16* v, int64_t bh, int64_t seq,
+                                const int32_t* ids, const float* log_weights, int64_t samples, const bf16* text_k,
+                                const bf16* text_v, int64_t text_tokens, bf16* o, float* lse, void* workspace,
+                                size_t workspace_bytes, cudaStream_t stream);
 cudaError_t launch_prefill_pair(const bf16* q, const bf16* k, const bf16* v, int64_t bh, int64_t seq,
                                 const int32_t* ids, const float* log_weights, int64_t samples, const bf16* text_k,
                                 const bf16* text_v, int64_t text_tokens, bf16* o, float* lse, void* workspace,

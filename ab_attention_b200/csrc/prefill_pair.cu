@@ -754,60 +754,82 @@ bool pair_supported(int64_t seq, int64_t samples, int64_t text_tokens) {
     return plan_smem_bytes(seq / kKv4, samples) <= 200 * 1024;
 }
 
-cudaError_t launch_prefill_pair(const bf16* q, const bf16* k, const bf16* v, int64_t bh, int64_t seq,
-                                const int32_t* ids, const float* log_weights, int64_t samples, const bf16* text_k,
-                                const bf16* text_v, int64_t text_tokens, bf16* o, float* lse, void* workspace,
-                                size_t workspace_bytes, cudaStream_t stream) {
-    const int64_t qb = ceil_div(seq, kQueryBlock);
-    const int64_t pairs_per_head = ceil_div(qb, 2);
-    const int64_t pairs = bh * pairs_per_head;
-    const int64_t text_granules = ceil_div(text_tokens, kKv4);
-    const int64_t stride = pair_stride(samples, text_granules);
-    if (workspace_bytes < pair_workspace_bytes(bh, seq, samples, text_tokens)) return cudaErrorInvalidValue;
-    const uintptr_t ws = (reinterpret_cast<uintptr_t>(workspace) + 255) & ~static_cast<uintptr_t>(255);
-    int4* info = reinterpret_cast<int4*>(ws);
-    uint32_t* entries = reinterpret_cast<uint32_t*>(ws + static_cast<uintptr_t>(pairs) * 16);
-    int32_t* codes = reinterpret_cast<int32_t*>(entries + pairs * stride);
+namespace {
 
+struct PairLayout {
+    int64_t qb, pairs_per_head, pairs, text_granules, stride;
+    int4* info;
+    uint32_t* entries;
+    int32_t* codes;
+};
+
+PairLayout pair_layout(int64_t bh, int64_t seq, int64_t samples, int64_t text_tokens, void* workspace) {
+    PairLayout l{};
+    l.qb = ceil_div(seq, kQueryBlock);
+    l.pairs_per_head = ceil_div(l.qb, 2);
+    l.pairs = bh * l.pairs_per_head;
+    l.text_granules = ceil_div(text_tokens, kKv4);
+    l.stride = pair_stride(samples, l.text_granules);
+    const uintptr_t ws = (reinterpret_cast<uintptr_t>(workspace) + 255) & ~static_cast<uintptr_t>(255);
+    l.info = reinterpret_cast<int4*>(ws);
+    l.entries = reinterpret_cast<uint32_t*>(ws + static_cast<uintptr_t>(l.pairs) * 16);
+    l.codes = reinterpret_cast<int32_t*>(l.entries + l.pairs * l.stride);
+    return l;
+}
+
+}  // namespace
+
+cudaError_t launch_pair_plan(const int32_t* ids, int64_t bh, int64_t seq, int64_t samples, int64_t text_tokens,
+                             void* workspace, size_t workspace_bytes, cudaStream_t stream) {
+    if (workspace_bytes < pair_workspace_bytes(bh, seq, samples, text_tokens)) return cudaErrorInvalidValue;
+    const PairLayout l = pair_layout(bh, seq, samples, text_tokens, workspace);
     PairPlanArgs plan{};
     plan.ids = ids;
-    plan.entries = entries;
-    plan.codes = codes;
-    plan.info = info;
-    plan.qb = qb;
-    plan.stride = stride;
-    plan.pairs_per_head = static_cast<int>(pairs_per_head);
+    plan.entries = l.entries;
+    plan.codes = l.codes;
+    plan.info = l.info;
+    plan.qb = l.qb;
+    plan.stride = l.stride;
+    plan.pairs_per_head = static_cast<int>(l.pairs_per_head);
     plan.samples = static_cast<int>(samples);
     plan.fine_blocks = static_cast<int>(seq / kKv4);
-    plan.text_granules = static_cast<int>(text_granules);
+    plan.text_granules = static_cast<int>(l.text_granules);
     plan.text_tail = static_cast<int>(text_tokens % kKv4);
     const size_t plan_smem = plan_smem_bytes(seq / kKv4, samples);
     cudaError_t err = cudaFuncSetAttribute(pair_plan_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                            static_cast<int>(plan_smem));
     if (err != cudaSuccess) return err;
-    pair_plan_kernel<<<static_cast<unsigned>(pairs), kPlanThreads, plan_smem, stream>>>(plan);
-    if ((err = cudaGetLastError()) != cudaSuccess) return err;
+    pair_plan_kernel<<<static_cast<unsigned>(l.pairs), kPlanThreads, plan_smem, stream>>>(plan);
+    return cudaGetLastError();
+}
 
+cudaError_t launch_pair_prefill(const bf16* q, const bf16* k, const bf16* v, int64_t bh, int64_t seq,
+                                const int32_t* ids, const float* log_weights, int64_t samples, const bf16* text_k,
+                                const bf16* text_v, int64_t text_tokens, bf16* o, float* lse, void* workspace,
+                                size_t workspace_bytes, cudaStream_t stream) {
+    if (workspace_bytes < pair_workspace_bytes(bh, seq, samples, text_tokens)) return cudaErrorInvalidValue;
+    const PairLayout l = pair_layout(bh, seq, samples, text_tokens, workspace);
     PairArgs args{};
     args.ids = ids;
     args.logw = log_weights;
-    args.entries = entries;
-    args.codes = codes;
-    args.info = info;
+    args.entries = l.entries;
+    args.codes = l.codes;
+    args.info = l.info;
     args.o = o;
     args.lse = lse;
     args.seq = seq;
-    args.qb = qb;
-    args.stride = stride;
+    args.qb = l.qb;
+    args.stride = l.stride;
     args.text_tokens = text_tokens;
     args.kv_rows = bh * seq;
-    args.pairs_per_head = static_cast<int>(pairs_per_head);
+    args.pairs_per_head = static_cast<int>(l.pairs_per_head);
     args.samples = static_cast<int>(samples);
     args.fine_blocks = static_cast<int>(seq / kKv4);
     args.text_tail = static_cast<int>(text_tokens % kKv4);
     args.kappa = qk_scale_log2();
     args.error = device_error_word();
     PairMaps maps;
+    cudaError_t err;
     if ((err = encode_rows(&maps.q, q, bh * seq, 128)) != cudaSuccess) return err;
     const bool has_text = text_tokens > 0 && text_k != nullptr && text_v != nullptr;
     const void* sources[2][2] = {{k, has_text ? text_k : k}, {v, has_text ? text_v : v}};
@@ -823,8 +845,18 @@ cudaError_t launch_prefill_pair(const bf16* q, const bf16* k, const bf16* v, int
     if (static_cast<int64_t>(attr.numRegs) * kThreads <
         static_cast<int64_t>(8 * 32 * kSoftmaxRegs + (kThreads - 8 * 32) * kProducerRegs))
         return cudaErrorInvalidConfiguration;
-    prefill_pair_kernel<<<static_cast<unsigned>(pairs), kThreads, kSmemBytes, stream>>>(args, maps);
+    prefill_pair_kernel<<<static_cast<unsigned>(l.pairs), kThreads, kSmemBytes, stream>>>(args, maps);
     return cudaGetLastError();
+}
+
+cudaError_t launch_prefill_pair(const bf16* q, const bf16* k, const bf16* v, int64_t bh, int64_t seq,
+                                const int32_t* ids, const float* log_weights, int64_t samples, const bf16* text_k,
+                                const bf16* text_v, int64_t text_tokens, bf16* o, float* lse, void* workspace,
+                                size_t workspace_bytes, cudaStream_t stream) {
+    cudaError_t err = launch_pair_plan(ids, bh, seq, samples, text_tokens, workspace, workspace_bytes, stream);
+    if (err != cudaSuccess) return err;
+    return launch_pair_prefill(q, k, v, bh, seq, ids, log_weights, samples, text_k, text_v, text_tokens, o, lse,
+                               workspace, workspace_bytes, stream);
 }
 
 }  // namespace abx

@@ -53,6 +53,13 @@ CONFIGS = {
 }
 
 
+# the CPU plumbing case, run through the reference math
+# in PyTorch on the host only (D = 64 and fp32 are outside the kernels' contract;
+# "2 deterministic + 6 sampled pages" is sample_pages = 8, the pi = 1 units coming
+# out of the certainty loop as in the reference).
+CPU_PLUMBING = VideoShape("cpu-plumbing", 1, 2, 4, 32, 32, 8, 0, dim=64)
+
+
 def smooth_field(batch_heads: int, frames: int, height: int, width: int, *, dim: int = 128,
                  seed: int = 0, sigma: float = 0.1, device="cuda", dtype=torch.bfloat16,
                  features: int = 16, heads: range | None = None):

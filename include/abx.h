@@ -155,6 +155,22 @@ int abx_sparse_prefill_paired(const void* q, const void* k, const void* v, int64
                               void* o, float* lse, void* workspace, size_t workspace_bytes,
                               abx_stream_t stream);
 
+/* The two launches of abx_sparse_prefill_paired as separate calls (no
+ * counterpart in the reference). abx_pair_plan writes each pair's union list
+ * for `ids` into the workspace; abx_sparse_prefill_paired_planned runs the
+ * prefill from those lists, which must have been written by abx_pair_plan for
+ * the same ids, shape and text count (the kernel range-checks every list entry,
+ * so stale lists give wrong results and ABX_ERR_INVALID_ARGUMENT, never an
+ * out-of-bounds read). A plan reused over several calls (the video schedule
+ * keeps a plan for four denoising steps) builds its lists once. Both return
+ * ABX_ERR_UNSUPPORTED for a shape abx_prefill_workspace_size reports as 0. */
+int abx_pair_plan(const int32_t* ids, int64_t bh, int64_t seq, int64_t samples, int64_t text_tokens,
+                  void* workspace, size_t workspace_bytes, abx_stream_t stream);
+int abx_sparse_prefill_paired_planned(const void* q, const void* k, const void* v, int64_t bh, int64_t seq,
+                                      const int32_t* ids, const float* log_weights, int64_t samples,
+                                      const void* text_k, const void* text_v, int64_t text_tokens, void* o,
+                                      float* lse, void* workspace, size_t workspace_bytes, abx_stream_t stream);
+
 /* Dense attention through the same prefill kernel (every KV4 block, shift 0):
  * the dense comparator. o / lse as above. */
 int abx_dense_prefill(const void* q, const void* k, const void* v, int64_t bh, int64_t seq,

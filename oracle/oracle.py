@@ -133,6 +133,30 @@ def sip(scores: np.ndarray, offsets: np.ndarray, samples: int):
 
 # ---- prefill -----------------------------------------------------------------
 
+def prefill_row(qh, kh, vh, row_ids, row_weights, r, text_k=None, text_v=None):
+    """One plan row (query block r of one head) of the float64 HT estimator:
+    keys are tokens 4*id + 0..3 of the row's granules, each with logit shift
+    log_weights[slot] (flashinfer_backend.py:30-58), followed by the always-
+    included text keys (shift 0); logits scaled by D^-1/2 * log2(e) (D = 128 in
+    the reference). Returns (o [n, D], lse [n]) for the block's n = min(128,
+    seq - 128 r) queries."""
+    kappa = qh.shape[-1] ** -0.5 * math.log2(math.e)
+    tok = (4 * np.asarray(row_ids, dtype=np.int64)[:, None] + np.arange(4)[None, :]).reshape(-1)
+    keys = np.asarray(kh[tok], dtype=np.float64)
+    vals = np.asarray(vh[tok], dtype=np.float64)
+    w = np.repeat(np.asarray(row_weights, dtype=np.float64), 4)
+    if text_k is not None:
+        keys = np.concatenate([keys, np.asarray(text_k, dtype=np.float64)])
+        vals = np.concatenate([vals, np.asarray(text_v, dtype=np.float64)])
+        w = np.concatenate([w, np.zeros(len(text_k))])
+    qs = np.asarray(qh[r * 128:(r + 1) * 128], dtype=np.float64)
+    logits = qs @ keys.T * kappa + w[None, :]
+    m = logits.max(axis=1, keepdims=True)
+    p = np.exp2(logits - m)
+    s = p.sum(axis=1, keepdims=True)
+    return (p @ vals) / s, (m + np.log2(s))[:, 0]
+
+
 def prefill(q, k, v, ids, log_weights, text_k=None, text_v=None):
     """Float64 evaluation of the HT-weighted sparse prefill.
 
@@ -143,31 +167,18 @@ def prefill(q, k, v, ids, log_weights, text_k=None, text_v=None):
     """
     bh, seq, dim = q.shape
     qb = math.ceil(seq / 128)
-    kappa = 128 ** -0.5 * math.log2(math.e)
     o = np.zeros((bh, seq, dim))
     lse = np.zeros((bh, seq))
-    offs = np.arange(4)
     for h in range(bh):
         qh = np.asarray(q[h], dtype=np.float64)
         kh = np.asarray(k[h], dtype=np.float64)
         vh = np.asarray(v[h], dtype=np.float64)
         for r in range(qb):
             row = h * qb + r
-            tok = (4 * ids[row][:, None] + offs[None, :]).reshape(-1)
-            keys = kh[tok]
-            vals = vh[tok]
-            w = np.repeat(log_weights[row].astype(np.float64), 4)
-            if text_k is not None:
-                keys = np.concatenate([keys, text_k[h].astype(np.float64)])
-                vals = np.concatenate([vals, text_v[h].astype(np.float64)])
-                w = np.concatenate([w, np.zeros(text_k.shape[1])])
-            qs = qh[r * 128:(r + 1) * 128]
-            logits = qs @ keys.T * kappa + w[None, :]
-            m = logits.max(axis=1, keepdims=True)
-            p = np.exp2(logits - m)
-            s = p.sum(axis=1, keepdims=True)
-            o[h, r * 128:r * 128 + len(qs)] = (p @ vals) / s
-            lse[h, r * 128:r * 128 + len(qs)] = (m + np.log2(s))[:, 0]
+            oo, ll = prefill_row(qh, kh, vh, ids[row], log_weights[row], r,
+                                 None if text_k is None else text_k[h], None if text_v is None else text_v[h])
+            o[h, r * 128:r * 128 + len(oo)] = oo
+            lse[h, r * 128:r * 128 + len(oo)] = ll
     return o, lse
 
 

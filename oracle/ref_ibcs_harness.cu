@@ -10,7 +10,49 @@
 // (the include path points at the reference checkout; nothing is copied) and
 // launches each stage kernel on its own, with the same launch shapes the
 // reference wrapper uses (csrc/ibcs.cu:589-614).
+//
+// Cluster assignments: the reference keeps each query's centroid slot in a
+// shared-memory array (`assignments`, csrc/ibcs.cu:116,165-197) and never
+// writes it out. To read it without copying or editing the reference source,
+// this unit compiles that source with one hook: every `__syncthreads()` in its
+// text becomes a barrier followed by a store of the kernel's `assignments`
+// array (when a dump buffer is set). Inside cluster_queries_kernel the name
+// refers to the kernel's own 128-entry shared array, which shadows the
+// one-element namespace-scope stand-in below; in every other kernel it refers
+// to the stand-in, whose size disables the store at compile time. The last
+// barrier of the kernel (after the populations, csrc/ibcs.cu:211) leaves the
+// final assignments in the dump. Headers are included first, so the hook
+// reaches only the reference file's own text, not CUB or the CUDA headers.
+#include <ATen/cuda/CUDAContext.h>
+#include <c10/cuda/CUDAException.h>
+#include <c10/cuda/CUDAGuard.h>
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cub/block/block_reduce.cuh>
+#include <torch/extension.h>
+
+#include "ops.h"
+#include "flashinfer/permuted_smem.cuh"
+
+namespace abx_ref_hook {
+__device__ int* g_assign_dump = nullptr;
+
+template <size_t kBytes>
+__device__ __forceinline__ void sync_and_dump(const int* values) {
+    __syncthreads();
+    if constexpr (kBytes == 128 * sizeof(int)) {
+        int* dump = g_assign_dump;
+        if (dump != nullptr && blockDim.x == 128)
+            dump[(static_cast<size_t>(blockIdx.y) * gridDim.x + blockIdx.x) * 128 + threadIdx.x] = values[threadIdx.x];
+    }
+}
+}  // namespace abx_ref_hook
+
+__device__ int assignments[1];  // stand-in, shadowed inside cluster_queries_kernel
+
+#define __syncthreads() abx_ref_hook::sync_and_dump<sizeof(assignments)>(assignments)
 #include "ibcs.cu"
+#undef __syncthreads
 
 #include <tuple>
 
@@ -29,6 +71,27 @@ std::tuple<torch::Tensor, torch::Tensor> cluster(torch::Tensor q) {
         tensor_ptr<const Bf16>(q), tensor_ptr<Bf16>(packed_q), tensor_ptr<half>(pops), seq, qb);
     C10_CUDA_KERNEL_LAUNCH_CHECK();
     return {packed_q, pops};
+}
+
+std::tuple<torch::Tensor, torch::Tensor, torch::Tensor> cluster_assignments(torch::Tensor q) {
+    // cluster() plus the per-query centroid slot [BH, qb, 128] int32 read out of
+    // the kernel's shared memory by the hook above; entries past a partial last
+    // block are unspecified (the reference never sets them).
+    TORCH_CHECK(q.is_cuda() && q.is_contiguous() && q.dim() == 3 && q.size(2) == kHeadDim);
+    const int64_t bh = q.size(0), seq = q.size(1);
+    const int64_t qb = (seq + kQueryBlockSize - 1) / kQueryBlockSize;
+    c10::cuda::CUDAGuard guard(q.device());
+    auto assign = torch::full({bh, qb, kQueryBlockSize}, -1, q.options().dtype(torch::kInt32));
+    auto stream = at::cuda::getCurrentCUDAStream();
+    int* dump = assign.data_ptr<int>();
+    C10_CUDA_CHECK(cudaMemcpyToSymbolAsync(abx_ref_hook::g_assign_dump, &dump, sizeof(dump), 0,
+                                           cudaMemcpyHostToDevice, stream));
+    auto out = cluster(q);
+    int* none = nullptr;
+    C10_CUDA_CHECK(cudaMemcpyToSymbolAsync(abx_ref_hook::g_assign_dump, &none, sizeof(none), 0,
+                                           cudaMemcpyHostToDevice, stream));
+    C10_CUDA_CHECK(cudaStreamSynchronize(stream));
+    return {std::get<0>(out), std::get<1>(out), assign};
 }
 
 torch::Tensor pool(torch::Tensor k) {
