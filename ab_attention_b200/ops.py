@@ -265,6 +265,49 @@ def sparse_prefill(q3, k3, v3, ids, logw, *, text_k=None, text_v=None, return_ls
     return o, lse_
 
 
+def prefill_workspace(bh: int, seq: int, samples: int, text_tokens: int, device) -> torch.Tensor | None:
+    """Workspace for the paired prefill's union lists, or None when the shape
+    cannot be paired (abx_prefill_workspace_size reports 0)."""
+    size = ctypes.c_size_t(0)
+    lib = _lib.load()
+    _lib.check(lib.abx_prefill_workspace_size(bh, seq, samples, text_tokens, ctypes.byref(size)),
+               "abx_prefill_workspace_size")
+    return torch.empty(size.value, dtype=torch.uint8, device=device) if size.value else None
+
+
+def pair_plan(ids: torch.Tensor, bh: int, seq: int, workspace: torch.Tensor, text_tokens: int = 0) -> None:
+    """Union lists of each pair of adjacent query blocks for `ids` [rows, samples]
+    into `workspace` (from prefill_workspace); a plan reused over several calls
+    builds them once and then runs sparse_prefill_planned."""
+    rows = bh * math.ceil(seq / QUERY_BLOCK)
+    if ids.ndim != 2:
+        raise RuntimeError("ids must be [rows, samples]")
+    _expect(ids, "ids", (rows, ids.shape[1]), torch.int32)
+    _expect(workspace, "workspace", (workspace.numel(),), torch.uint8)
+    _one_device(ids, workspace)
+    lib = _lib.load()
+    with torch.cuda.device(ids.device):
+        _lib.check(lib.abx_pair_plan(_lib.ptr(ids), bh, seq, ids.shape[1], text_tokens, _lib.ptr(workspace),
+                                     workspace.numel(), _lib.stream_of(ids)), "abx_pair_plan")
+
+
+def sparse_prefill_planned(q3, k3, v3, ids, logw, workspace, *, text_k=None, text_v=None, return_lse=False):
+    """The paired prefill from union lists already written by pair_plan for these ids."""
+    _check_attention_inputs(q3, k3, v3, ids, logw, text_k, text_v)
+    _expect(workspace, "workspace", (workspace.numel(),), torch.uint8)
+    bh, seq, _ = q3.shape
+    o = torch.empty_like(q3)
+    lse_ = torch.empty((bh, seq), dtype=torch.float32, device=q3.device) if return_lse else None
+    text_tokens = 0 if text_k is None else text_k.shape[1]
+    lib = _lib.load()
+    with torch.cuda.device(q3.device):
+        _lib.check(lib.abx_sparse_prefill_paired_planned(
+            _lib.ptr(q3), _lib.ptr(k3), _lib.ptr(v3), bh, seq, _lib.ptr(ids), _lib.ptr(logw), ids.shape[1],
+            _lib.ptr(text_k), _lib.ptr(text_v), text_tokens, _lib.ptr(o), _lib.ptr(lse_), _lib.ptr(workspace),
+            workspace.numel(), _lib.stream_of(q3)), "abx_sparse_prefill_paired_planned")
+    return o, lse_
+
+
 def dense_prefill(q3, k3, v3, *, return_lse=False):
     """Dense attention through the same prefill kernel (the dense comparator)."""
     _check_attention_inputs(q3, k3, v3)

@@ -89,7 +89,7 @@ def gather_block(out: torch.Tensor, local_block: torch.Tensor, world: int, block
 
 
 def attention_sharded(q, k, v, offsets, out, *, world: int, chunks: int, sample_pages: int = 64,
-                      text_kv=None, group=None):
+                      text_kv=None, group=None, timing: dict | None = None):
     """This rank's part of a head-sharded AB-attention layer.
 
     q, k, v: [1, per, S, 128] bf16, the rank's heads in `rank_heads(BH, world,
@@ -98,6 +98,11 @@ def attention_sharded(q, k, v, offsets, out, *, world: int, chunks: int, sample_
     The plan covers all the rank's heads in one call; the prefill runs block
     by block and block c is all-gathered on NCCL's stream while block c + 1
     computes. Returns when `out` is complete on the current stream.
+
+    `timing` (a dict, optional) receives CUDA events recorded on the current
+    stream: "plan" (start, end), "blocks" [(start, end)] around each block's
+    prefill, and "tail" (after the last prefill, after the last all-gather
+    has landed), whose span is the all-gather time left exposed.
     """
     from .attention import SamplePlan, apply_plan, build_plan
 
@@ -106,18 +111,35 @@ def attention_sharded(q, k, v, offsets, out, *, world: int, chunks: int, sample_
         raise ValueError(f"{per} local heads do not split into {chunks} blocks")
     ch = per // chunks
     qb = math.ceil(tokens / 128)
+
+    def event():
+        e = torch.cuda.Event(enable_timing=True)
+        e.record()
+        return e
+
+    if timing is not None:
+        timing["blocks"] = []
+        plan_start = event()
     plan = build_plan(q, k, sample_pages=sample_pages, offsets=offsets)
+    if timing is not None:
+        timing["plan"] = (plan_start, event())
     works = []
     for c in range(chunks):
         heads = slice(c * ch, (c + 1) * ch)
         rows = slice(c * ch * qb, (c + 1) * ch * qb)
         block_plan = SamplePlan(plan.descriptor[rows], plan.log_weights[rows])
         block_text = None if text_kv is None else tuple(t[:, heads] for t in text_kv)
+        start = event() if timing is not None else None
         o = apply_plan(q[:, heads], k[:, heads], v[:, heads], block_plan, text_kv=block_text)
+        if timing is not None:
+            timing["blocks"].append((start, event()))
         works.append(gather_block(out, o.reshape(ch, tokens, q.shape[3]), world, c, group=group, async_op=True))
+    tail_start = event() if timing is not None else None
     for work in works:
         if work is not None:
             work.wait()
+    if timing is not None:
+        timing["tail"] = (tail_start, event())
     return out
 
 
