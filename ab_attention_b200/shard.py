@@ -7,12 +7,16 @@ layer from the seed (as the reference draws them before chunking,
 ab_attention/attention.py:56-57) and sliced, so the plan is bit-identical for
 any number of GPUs. The output is reassembled with NCCL all-gathers.
 
-Heads are dealt to ranks in chunks so that the all-gathers overlap compute: the
-layer's heads form `chunks` consecutive blocks of world * ch heads; rank r owns
-heads [(c * world + r) * ch, (c * world + r + 1) * ch) of block c. A rank builds
-the plan for all its heads at once, then runs the sparse prefill block by block
-and all-gathers block c (straight into its place in the [BH, S, 128] output)
-while block c + 1 computes.
+Heads are dealt to ranks in blocks so that the all-gathers overlap compute: the
+layer's heads form consecutive blocks, block c holding world * b_c heads, of
+which rank r owns [start_c + r * b_c, start_c + (r + 1) * b_c). The blocks are
+either even (`chunks` blocks of the same size) or tapered (`taper_sizes`: the
+largest first and one head per rank last, so the all-gather left exposed after
+the last prefill is the smallest). A rank builds the plan for all its heads at
+once, then runs the sparse prefill block by block and all-gathers block c
+(straight into its place in the [BH, S, 128] output) while block c + 1
+computes; consecutive blocks' prefills go to two alternating streams, so a
+block's launch fills the SMs that the previous block's last wave leaves idle.
 """
 from __future__ import annotations
 
@@ -34,12 +38,53 @@ def chunk_count(batch_heads: int, world: int, max_chunks: int = 8) -> int:
     return 1
 
 
-def rank_heads(batch_heads: int, world: int, rank: int, chunks: int = 1) -> list[int]:
-    """The flattened heads rank `rank` owns, in its local (block-major) order."""
-    if batch_heads % (world * chunks):
-        raise ValueError(f"{batch_heads} heads do not split into {chunks} blocks over {world} ranks")
-    ch = batch_heads // (world * chunks)
-    return [(c * world + rank) * ch + i for c in range(chunks) for i in range(ch)]
+def taper_sizes(per_rank: int, max_blocks: int = 8) -> list[int]:
+    """Heads per rank in each block, non-increasing and ending with one head:
+    1, 2, ..., n from the end (n(n + 1)/2 <= per_rank, n <= max_blocks), the
+    remainder as one more block or, at the block limit, one head more on each of
+    the largest blocks. Each block's all-gather then hides under the next,
+    smaller block's prefill (a head's gather over NVLink takes well under half
+    its prefill) and the gather left exposed at the end is one head per rank."""
+    if per_rank <= 0 or max_blocks <= 0:
+        raise ValueError("a rank needs at least one head and one block")
+    n = 1
+    while n + 1 <= max_blocks and (n + 1) * (n + 2) // 2 <= per_rank:
+        n += 1
+    sizes = list(range(n, 0, -1))
+    rest = per_rank - n * (n + 1) // 2
+    if rest and n < max_blocks:
+        sizes.append(rest)
+    else:
+        for i in range(rest):
+            sizes[i % n] += 1
+    return sorted(sizes, reverse=True)
+
+
+def block_sizes(batch_heads: int, world: int, chunks) -> list[int]:
+    """Heads per rank in each block: `chunks` is a block count (even blocks) or
+    the list of sizes itself."""
+    if batch_heads % world:
+        raise ValueError(f"{batch_heads} heads do not split evenly over {world} ranks")
+    per = batch_heads // world
+    if isinstance(chunks, int):
+        if per % chunks:
+            raise ValueError(f"{batch_heads} heads do not split into {chunks} blocks over {world} ranks")
+        return [per // chunks] * chunks
+    sizes = [int(c) for c in chunks]
+    if any(c <= 0 for c in sizes) or sum(sizes) != per:
+        raise ValueError(f"block sizes {sizes} do not cover the {per} heads of a rank")
+    return sizes
+
+
+def rank_heads(batch_heads: int, world: int, rank: int, chunks=1) -> list[int]:
+    """The flattened heads rank `rank` owns, in its local (block-major) order.
+    `chunks`: a block count (even blocks) or the per-rank block sizes."""
+    sizes = block_sizes(batch_heads, world, chunks)
+    heads, start = [], 0
+    for b in sizes:
+        heads.extend(start + rank * b + i for i in range(b))
+        start += world * b
+    return heads
 
 
 def head_slice(batch_heads: int, world: int, rank: int) -> slice:
@@ -75,29 +120,33 @@ def gather_heads(local: torch.Tensor, world: int, group=None) -> torch.Tensor:
 
 
 def gather_block(out: torch.Tensor, local_block: torch.Tensor, world: int, block: int, group=None,
-                 async_op: bool = False):
+                 async_op: bool = False, start: int | None = None):
     """All-gather block `block` (each rank's [ch, ...] heads) into its place in
-    `out` [BH, ...]: heads [block * world * ch, (block + 1) * world * ch)."""
+    `out` [BH, ...]: heads [start, start + world * ch), start = block * world * ch
+    for even blocks (pass `start` for uneven ones)."""
     import torch.distributed as dist
 
     ch = local_block.shape[0]
-    dst = out[block * world * ch:(block + 1) * world * ch]
+    first = block * world * ch if start is None else start
+    dst = out[first:first + world * ch]
     if world == 1:
         dst.copy_(local_block)
         return None
     return dist.all_gather_into_tensor(dst, local_block.contiguous(), group=group, async_op=async_op)
 
 
-def attention_sharded(q, k, v, offsets, out, *, world: int, chunks: int, sample_pages: int = 64,
-                      text_kv=None, group=None, timing: dict | None = None):
+def attention_sharded(q, k, v, offsets, out, *, world: int, chunks, sample_pages: int = 64,
+                      text_kv=None, group=None, timing: dict | None = None, block_streams: int = 2):
     """This rank's part of a head-sharded AB-attention layer.
 
     q, k, v: [1, per, S, 128] bf16, the rank's heads in `rank_heads(BH, world,
-    rank, chunks)` order; offsets: their rows of `layer_offsets` (see
-    `shard_offsets`); out: [BH, S, 128] bf16, receives every rank's output.
-    The plan covers all the rank's heads in one call; the prefill runs block
-    by block and block c is all-gathered on NCCL's stream while block c + 1
-    computes. Returns when `out` is complete on the current stream.
+    rank, chunks)` order (`chunks`: a block count or the per-rank block sizes);
+    offsets: their rows of `layer_offsets` (see `shard_offsets`); out: [BH, S,
+    128] bf16, receives every rank's output. The plan covers all the rank's
+    heads in one call; the prefill runs block by block, consecutive blocks on
+    `block_streams` alternating streams, and block c is all-gathered on NCCL's
+    stream while block c + 1 computes. Returns when `out` is complete on the
+    current stream.
 
     `timing` (a dict, optional) receives CUDA events recorded on the current
     stream: "plan" (start, end), "blocks" [(start, end)] around each block's
@@ -107,33 +156,44 @@ def attention_sharded(q, k, v, offsets, out, *, world: int, chunks: int, sample_
     from .attention import SamplePlan, apply_plan, build_plan
 
     per, tokens = q.shape[1], q.shape[2]
-    if per % chunks:
-        raise ValueError(f"{per} local heads do not split into {chunks} blocks")
-    ch = per // chunks
+    sizes = block_sizes(per * world, world, chunks)
     qb = math.ceil(tokens / 128)
+    main = torch.cuda.current_stream(q.device)
+    streams = [main] + [torch.cuda.Stream(q.device) for _ in range(max(1, block_streams) - 1)]
 
-    def event():
+    def event(stream=None):
         e = torch.cuda.Event(enable_timing=True)
-        e.record()
+        e.record(stream or main)
         return e
 
     if timing is not None:
         timing["blocks"] = []
         plan_start = event()
     plan = build_plan(q, k, sample_pages=sample_pages, offsets=offsets)
+    planned = event()
     if timing is not None:
-        timing["plan"] = (plan_start, event())
+        timing["plan"] = (plan_start, planned)
     works = []
-    for c in range(chunks):
-        heads = slice(c * ch, (c + 1) * ch)
-        rows = slice(c * ch * qb, (c + 1) * ch * qb)
+    first = local = 0
+    for c, ch in enumerate(sizes):
+        stream = streams[c % len(streams)]
+        heads = slice(local, local + ch)
+        rows = slice(local * qb, (local + ch) * qb)
         block_plan = SamplePlan(plan.descriptor[rows], plan.log_weights[rows])
         block_text = None if text_kv is None else tuple(t[:, heads] for t in text_kv)
-        start = event() if timing is not None else None
-        o = apply_plan(q[:, heads], k[:, heads], v[:, heads], block_plan, text_kv=block_text)
-        if timing is not None:
-            timing["blocks"].append((start, event()))
-        works.append(gather_block(out, o.reshape(ch, tokens, q.shape[3]), world, c, group=group, async_op=True))
+        stream.wait_event(planned)
+        with torch.cuda.stream(stream):
+            start = event(stream) if timing is not None else None
+            o = apply_plan(q[:, heads], k[:, heads], v[:, heads], block_plan, text_kv=block_text)
+            if timing is not None:
+                timing["blocks"].append((start, event(stream)))
+            # issued from the block's stream, so NCCL waits for this block only
+            works.append(gather_block(out, o.reshape(ch, tokens, q.shape[3]), world, c, group=group,
+                                      async_op=True, start=first))
+        first += world * ch
+        local += ch
+    for stream in streams[1:]:
+        main.wait_stream(stream)
     tail_start = event() if timing is not None else None
     for work in works:
         if work is not None:
@@ -148,7 +208,8 @@ def attention_sharded_host(q, k, v, offsets, out, host_out, *, world: int, chunk
     """`attention_sharded` for Q/K/V in host memory, with the copies overlapped.
 
     q, k, v: pinned host [1, per, S, 128] bf16, the rank's heads in
-    `rank_heads(BH, world, rank, chunks)` order; offsets: their rows of
+    `rank_heads(BH, world, rank, chunks)` order (`chunks`: a block count or the
+    per-rank block sizes); offsets: their rows of
     `layer_offsets` on the device; out: [BH, S, 128] bf16 on the device,
     receives every rank's output; host_out: pinned host [1, per, S, 128],
     receives this rank's heads. text_kv (optional): the rank's prompt keys and
@@ -165,13 +226,13 @@ def attention_sharded_host(q, k, v, offsets, out, host_out, *, world: int, chunk
     from .attention import apply_plan, build_plan
 
     per, tokens, dim = q.shape[1], q.shape[2], q.shape[3]
-    if per % chunks:
-        raise ValueError(f"{per} local heads do not split into {chunks} blocks")
+    sizes = block_sizes(per * world, world, chunks)
     if q.device.type != "cpu" or k.device.type != "cpu" or v.device.type != "cpu" or host_out.device.type != "cpu":
         raise ValueError("q, k, v and host_out must be host tensors")
     if host_out.shape != q.shape or host_out.dtype != q.dtype:
         raise ValueError("host_out must be shaped like q")
-    ch = per // chunks
+    ch = max(sizes)
+    starts = [sum(sizes[:c]) for c in range(len(sizes))]
     qb = math.ceil(tokens / 128)
     device = out.device
     main = torch.cuda.current_stream(device)
@@ -184,32 +245,33 @@ def attention_sharded_host(q, k, v, offsets, out, host_out, *, world: int, chunk
     freed = [torch.cuda.Event() for _ in range(2)]
 
     def load(c):
-        s = c % 2
+        s, b, h0 = c % 2, sizes[c], starts[c]
         with torch.cuda.stream(copy_in):
             if c >= 2:
                 copy_in.wait_event(freed[s])  # the slot's previous block has been consumed
             for dst, src in zip(slots[s], (q, k, v)):
-                dst.copy_(src[:, c * ch:(c + 1) * ch], non_blocking=True)
+                dst[:, :b].copy_(src[:, h0:h0 + b], non_blocking=True)
             landed[s].record(copy_in)
 
     works = []
     load(0)
-    for c in range(chunks):
-        if c + 1 < chunks:
+    for c, b in enumerate(sizes):
+        if c + 1 < len(sizes):
             load(c + 1)
-        s = c % 2
+        s, h0 = c % 2, starts[c]
         main.wait_event(landed[s])
-        qs, ks, vs = slots[s]
-        plan = build_plan(qs, ks, sample_pages=sample_pages, offsets=offsets[c * ch * qb:(c + 1) * ch * qb])
-        block_text = None if text_kv is None else tuple(t[:, c * ch:(c + 1) * ch] for t in text_kv)
+        qs, ks, vs = (x[:, :b] for x in slots[s])
+        plan = build_plan(qs, ks, sample_pages=sample_pages, offsets=offsets[h0 * qb:(h0 + b) * qb])
+        block_text = None if text_kv is None else tuple(t[:, h0:h0 + b] for t in text_kv)
         o = apply_plan(qs, ks, vs, plan, text_kv=block_text)
         freed[s].record(main)
-        works.append(gather_block(out, o.reshape(ch, tokens, dim), world, c, group=group, async_op=True))
+        works.append(gather_block(out, o.reshape(b, tokens, dim), world, c, group=group, async_op=True,
+                                  start=world * h0))
         done = torch.cuda.Event()
         done.record(main)
         with torch.cuda.stream(copy_out):
             copy_out.wait_event(done)
-            host_out[:, c * ch:(c + 1) * ch].copy_(o, non_blocking=True)
+            host_out[:, h0:h0 + b].copy_(o, non_blocking=True)
             o.record_stream(copy_out)
     for work in works:
         if work is not None:

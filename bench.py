@@ -295,7 +295,7 @@ def phase_times_sharded(shard, q, k, v, offsets, gathered, world, chunks, shape,
     return {
         "plan_ms": med(t["plan"][0].elapsed_time(t["plan"][1]) for t in samples),
         "prefill_ms_per_block": [med(t["blocks"][c][0].elapsed_time(t["blocks"][c][1]) for t in samples)
-                                 for c in range(chunks)],
+                                 for c in range(len(samples[0]["blocks"]))],
         "exposed_gather_ms": med(t["tail"][0].elapsed_time(t["tail"][1]) for t in samples),
         "prefill_and_gather_ms": med(t["plan"][1].elapsed_time(t["tail"][1]) for t in samples),
     }
@@ -396,7 +396,8 @@ def main() -> None:
     from ab_attention_b200 import shard
 
     bh = shape.batch_heads
-    chunks = shard.chunk_count(bh, world) if world > 1 else 1
+    # tapered head blocks (largest first, one head per rank last) on N > 1
+    chunks = shard.taper_sizes(bh // world) if world > 1 else 1
     heads = shard.rank_heads(bh, world, rank, chunks)
     per = len(heads)
     q, k, v, text = make_inputs(shape, device=device, bh_slice=heads if world > 1 else None)
@@ -559,8 +560,8 @@ def main() -> None:
                    "text_tokens": shape.text_tokens, "parallelism": f"heads{world}",
                    "l2": "inputs (Q/K/V 4.6 GB) larger than L2; no flush",
                    "step": "build_plan (fresh plan) + apply_plan"
-                           + (f" in {chunks} head blocks, each all-gathered while the next computes"
-                              if world > 1 else "")},
+                           + (f" in head blocks of {chunks} heads per rank, each all-gathered while the next "
+                              f"computes" if world > 1 else "")},
         "eff_tflops": eq_flops / (ms * 1e-3) / 1e12,
         "sparse_tflops": sparse_flops / (ms * 1e-3) / 1e12,
         "plan_ms": plan_ms, "prefill_ms": prefill_ms,
@@ -584,7 +585,7 @@ def main() -> None:
                                   "fast-math exp2/log2/division work and the double-precision SIP sums"},
         # cluster, pool, lse, sip + a pair plan and a prefill per head block per step
         # (NCCL's kernels not counted)
-        "gpu_launches": (3 + 2 * chunks) * args.steps,
+        "gpu_launches": (3 + 2 * (len(chunks) if world > 1 else 1)) * args.steps,
         "clocks": clocks.summary(),
         **dense,
     }

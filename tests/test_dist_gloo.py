@@ -145,3 +145,48 @@ def test_failed_rank_surfaces_as_error_not_hang(tmp_path):
     # rank 0 either recorded an error from the collective or never wrote a result
     if os.path.exists(path):
         assert torch.load(path)["status"].startswith("error")
+
+
+def test_taper_sizes_end_with_one_head_and_cover_the_rank():
+    for per in (1, 2, 3, 5, 10, 12, 20, 40, 80):
+        sizes = shard.taper_sizes(per)
+        assert sum(sizes) == per and len(sizes) <= 8
+        assert sizes == sorted(sizes, reverse=True)
+        if per <= 36:
+            assert sizes[-1] == 1
+    assert shard.taper_sizes(10) == [4, 3, 2, 1]
+
+
+@pytest.mark.parametrize("world,sizes", [(2, [2, 1, 1]), (4, [1, 1])])
+def test_uneven_blocks_partition_and_gather_in_place(tmp_path, world, sizes):
+    owned = sorted(h for r in range(world) for h in shard.rank_heads(BH, world, r, sizes))
+    assert owned == list(range(BH))
+    path = str(tmp_path / "out.pt")
+    mp.start_processes(_uneven_worker, args=(world, _free_port(), path, sizes), nprocs=world, join=True,
+                       start_method="spawn")
+    _, want = _reference()
+    assert torch.equal(torch.load(path)["full"], want)
+
+
+def _uneven_worker(rank, world, port, result_path, sizes):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=timedelta(seconds=10))
+    try:
+        x, _ = _reference()
+        heads = shard.rank_heads(BH, world, rank, sizes)
+        offsets = shard.shard_offsets(shard.layer_offsets(BH, TOKENS, SEED, "cpu"), TOKENS, heads)
+        qb = math.ceil(TOKENS / 128)
+        out = torch.empty_like(x)
+        works, local, first = [], 0, 0
+        for c, b in enumerate(sizes):
+            block = torch.stack([_per_head(x[heads[i]], offsets[i * qb:(i + 1) * qb])
+                                 for i in range(local, local + b)])
+            works.append(shard.gather_block(out, block, world, c, async_op=True, start=first))
+            local += b
+            first += world * b
+        for w in works:
+            w.wait()
+        if rank == 0:
+            torch.save({"status": "ok", "full": out}, result_path)
+    finally:
+        dist.destroy_process_group()

@@ -186,3 +186,27 @@ def test_sharded_host_pipeline_equals_device_path(with_text):
     torch.cuda.synchronize()
     assert torch.equal(out, want[0])
     assert torch.equal(host_out, want.cpu())
+
+
+@pytest.mark.parametrize("sizes,streams", [([2, 1, 1], 2), ([3, 1], 1), (4, 2)])
+def test_sharded_blocks_on_alternating_streams_equal_device_path(sizes, streams):
+    """attention_sharded run as one rank, with tapered or even head blocks whose
+    prefills alternate between streams, writes the device path's output bit for bit
+    (host pipeline likewise with uneven blocks)."""
+    from ab_attention_b200 import shard
+
+    heads = 4
+    q, k, v = (x.reshape(1, heads, -1, 128) for x in smooth_field(heads, 2, 16, 32, seed=14, device="cuda"))
+    tokens = q.shape[2]
+    offsets = shard.layer_offsets(heads, tokens, seed=4, device="cuda")
+    want = apply_plan(q, k, v, build_plan(q, k, sample_pages=2, offsets=offsets))
+    out = torch.zeros((heads, tokens, 128), dtype=torch.bfloat16, device="cuda")
+    shard.attention_sharded(q, k, v, offsets, out, world=1, chunks=sizes, sample_pages=2, block_streams=streams)
+    torch.cuda.synchronize()
+    assert torch.equal(out, want[0])
+    hq, hk, hv = (x.cpu().pin_memory() for x in (q, k, v))
+    host_out = torch.empty(q.shape, dtype=q.dtype).pin_memory()
+    out.zero_()
+    shard.attention_sharded_host(hq, hk, hv, offsets, out, host_out, world=1, chunks=sizes, sample_pages=2)
+    torch.cuda.synchronize()
+    assert torch.equal(out, want[0]) and torch.equal(host_out, want.cpu())
