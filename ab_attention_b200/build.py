@@ -22,6 +22,7 @@ ROOT = PKG.parent
 CSRC = PKG / "csrc"
 BUILD = PKG / "_build"
 LIB = PKG / "libabx.so"
+TORCH_LIB = PKG / "libabx_torch.so"  # torch.ops.ab_attention (csrc/torch_ops.cpp)
 SOURCES = ("ibcs.cu", "sip.cu", "prefill.cu", "prefill_pair.cu", "capi.cu")
 HEADERS = ("common.cuh", "ibcs.cuh", "tcgen05.cuh", "tma_host.cuh", "f32x2.cuh", "mix.cuh")
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
@@ -69,8 +70,30 @@ def build(force: bool = False, jobs: int = 4, verbose: bool = False) -> Path:
             if verbose and out:
                 print(out)
     if force or commands or _stale(LIB, objects):
-        run([nvcc(), "-shared", *ARCH, "-o", str(LIB), *map(str, objects)])
+        # a SONAME, so the torch operator library records it and finds it beside itself
+        run([nvcc(), "-shared", *ARCH, "-Xlinker", "-soname=libabx.so", "-o", str(LIB), *map(str, objects)])
+    build_torch_ops(force, run)
     return LIB
+
+
+def build_torch_ops(force: bool, run) -> Path:
+    """libabx_torch.so: the TORCH_LIBRARY(ab_attention) operators over the C ABI,
+    compiled against the installed torch and linked to libabx.so."""
+    import torch
+    from torch.utils import cpp_extension
+
+    src = CSRC / "torch_ops.cpp"
+    if not (force or _stale(TORCH_LIB, [src, LIB, ROOT / "include" / "abx.h"])):
+        return TORCH_LIB
+    abi = int(torch._C._GLIBCXX_USE_CXX11_ABI)
+    includes = [f"-I{p}" for p in [str(ROOT / "include"), *cpp_extension.include_paths("cuda")]]
+    libdirs = cpp_extension.library_paths("cuda")
+    cmd = [os.environ.get("CXX", "g++"), "-O2", "-std=c++17", "-shared", "-fPIC", f"-D_GLIBCXX_USE_CXX11_ABI={abi}",
+           *includes, str(src), "-o", str(TORCH_LIB), f"-L{PKG}", "-l:libabx.so",
+           *[f"-L{d}" for d in libdirs], "-ltorch", "-ltorch_cpu", "-ltorch_cuda", "-lc10", "-lc10_cuda",
+           "-Wl,-rpath,$ORIGIN", *[f"-Wl,-rpath,{d}" for d in libdirs]]
+    run(cmd)
+    return TORCH_LIB
 
 
 if __name__ == "__main__":

@@ -344,23 +344,17 @@ def cross_prefill(q3, k3, v3, *, ids=None, logw=None, samples=0, text_k=None, te
                    "abx_cross_prefill")
     return o, lse_
 
-# ---- torch.library registration ------------------------------------------------------
-# `torch.ops.ab_attention.{ibcs,sip,sparse_prefill}`: the custom-op form of the
-# same entry points, with a CUDA kernel only. A CPU tensor finds no kernel and
-# raises, so there is no silent fallback.
+# ---- torch.library operators ----------------------------------------------------------
+# `torch.ops.ab_attention.{ibcs, sip, build_plan, sparse_prefill}`: C++ operators
+# (csrc/torch_ops.cpp, TORCH_LIBRARY over the same C ABI) with CUDA and Meta
+# kernels only. A CPU tensor finds no kernel and raises, so there is no silent
+# fallback; C++ and TorchScript callers reach them without Python.
 
-@torch.library.custom_op("ab_attention::ibcs", mutates_args=(), device_types="cuda")
-def _ibcs_op(q: torch.Tensor, k: torch.Tensor) -> torch.Tensor:
-    return ibcs(q, k)
-
-
-@torch.library.custom_op("ab_attention::sip", mutates_args=("ids", "logs"), device_types="cuda")
-def _sip_op(scores: torch.Tensor, offsets: torch.Tensor, ids: torch.Tensor, logs: torch.Tensor) -> None:
-    sip(scores, offsets, ids, logs)
+def _load_torch_ops() -> None:
+    path = _lib.PKG / "libabx_torch.so"
+    if not path.exists():
+        raise ImportError(f"{path} is not built; run python -m ab_attention_b200.build")
+    torch.ops.load_library(str(path))
 
 
-@torch.library.custom_op("ab_attention::sparse_prefill", mutates_args=(), device_types="cuda")
-def _sparse_prefill_op(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, ids: torch.Tensor,
-                       log_weights: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
-    """[BH,S,128] bf16 q/k/v, ids/log_weights [rows, samples] -> (o, base-2 lse [BH,S])."""
-    return sparse_prefill(q, k, v, ids, log_weights, return_lse=True)
+_load_torch_ops()

@@ -173,3 +173,22 @@ def test_op_wrappers_check_buffers_before_passing_pointers():
     with pytest.raises(_lib.AbxError, match="CUDA"):
         ops.cross_prefill(q, None, None, samples=0, text_k=torch.zeros(2, 0, 128, dtype=bf),
                           text_v=torch.zeros(2, 0, 128, dtype=bf))
+
+
+def test_torch_operators_are_cpp_with_meta_shapes():
+    """torch.ops.ab_attention comes from the C++ TORCH_LIBRARY in libabx_torch.so; its
+    Meta kernels give output shapes without data (for tracers)."""
+    import torch
+
+    import ab_attention_b200  # noqa: F401
+
+    for name in ("ibcs", "sip", "build_plan", "sparse_prefill"):
+        assert hasattr(torch.ops.ab_attention, name)
+    q = torch.empty(2, 3, 1000, 128, dtype=torch.bfloat16, device="meta")
+    scores = torch.ops.ab_attention.ibcs(q, q)
+    assert scores.shape == (6 * 8, 250) and scores.dtype == torch.float32
+    ids, logw = torch.ops.ab_attention.build_plan(q, q, torch.empty(48, device="meta"), 64)
+    assert ids.shape == (48, 64) and ids.dtype == torch.int32 and logw.dtype == torch.float32
+    q3 = q.reshape(6, 1000, 128)
+    o, lse = torch.ops.ab_attention.sparse_prefill(q3, q3, q3, ids, logw)
+    assert o.shape == q3.shape and lse.shape == (6, 1000)

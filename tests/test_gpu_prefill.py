@@ -139,6 +139,8 @@ def test_torch_ops_and_paged_attention_match_python_api():
     logw2 = torch.empty_like(logw)
     torch.ops.ab_attention.sip(scores, offsets, ids2, logw2)
     assert torch.equal(ids2, ids) and torch.equal(logw2, logw)
+    ids3, logw3 = torch.ops.ab_attention.build_plan(q4, k4, offsets, ids.shape[1])
+    assert torch.equal(ids3, ids) and torch.equal(logw3, logw)
 
 
 @pytest.mark.parametrize("with_text", [False, True])
