@@ -15,8 +15,11 @@ largest first and one head per rank last, so the all-gather left exposed after
 the last prefill is the smallest). A rank builds the plan for all its heads at
 once, then runs the sparse prefill block by block and all-gathers block c
 (straight into its place in the [BH, S, 128] output) while block c + 1
-computes; consecutive blocks' prefills go to two alternating streams, so a
-block's launch fills the SMs that the previous block's last wave leaves idle.
+computes. Consecutive blocks' prefills can also alternate between streams
+(`block_streams`), so that a block's launch fills the SMs the previous block's
+last wave leaves idle; measured on 8 B200s this starves NCCL's all-gather
+kernels of SMs (the gathers then queue behind the prefills), so one stream is
+the default.
 """
 from __future__ import annotations
 
@@ -136,7 +139,7 @@ def gather_block(out: torch.Tensor, local_block: torch.Tensor, world: int, block
 
 
 def attention_sharded(q, k, v, offsets, out, *, world: int, chunks, sample_pages: int = 64,
-                      text_kv=None, group=None, timing: dict | None = None, block_streams: int = 2):
+                      text_kv=None, group=None, timing: dict | None = None, block_streams: int = 1):
     """This rank's part of a head-sharded AB-attention layer.
 
     q, k, v: [1, per, S, 128] bf16, the rank's heads in `rank_heads(BH, world,

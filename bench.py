@@ -277,7 +277,8 @@ def run_reference(args, shape) -> None:
 
 # ---- GPU arm -----------------------------------------------------------------------
 
-def phase_times_sharded(shard, q, k, v, offsets, gathered, world, chunks, shape, text, reps=3) -> dict:
+def phase_times_sharded(shard, q, k, v, offsets, gathered, world, chunks, shape, text, reps=3,
+                        block_streams: int = 1) -> dict:
     """Phases of a sharded step from events inside attention_sharded (median of
     `reps` untimed steps): the plan, each head block's prefill, and the
     all-gather time left exposed after the last block's prefill."""
@@ -288,7 +289,8 @@ def phase_times_sharded(shard, q, k, v, offsets, gathered, world, chunks, shape,
         dist.barrier()
         timing = {}
         shard.attention_sharded(q, k, v, offsets, gathered, world=world, chunks=chunks,
-                                sample_pages=shape.sample_pages, text_kv=text, timing=timing)
+                                sample_pages=shape.sample_pages, text_kv=text, timing=timing,
+                                block_streams=block_streams)
         torch.cuda.synchronize()
         samples.append(timing)
     med = statistics.median
@@ -348,6 +350,12 @@ def main() -> None:
     parser.add_argument("--no-cpu-baseline", action="store_true")
     parser.add_argument("--no-dense", action="store_true")
     parser.add_argument("--no-e2e", action="store_true")
+    parser.add_argument("--shard-blocks", default="even", choices=["even", "taper"],
+                        help="N > 1: head blocks of equal size, or tapered to one head per rank last")
+    parser.add_argument("--block-streams", type=int, default=1,
+                        help="N > 1: streams the head blocks' prefills alternate between")
+    parser.add_argument("--nccl-priority", default="normal", choices=["normal", "high"],
+                        help="N > 1: priority of NCCL's stream")
     parser.add_argument("--no-ref-kernels", action="store_true",
                         help="reference arm: skip timing the reference's own IBCS/SIP kernels on the GPU")
     parser.add_argument("--sample-pages", type=int, default=0,
@@ -386,7 +394,12 @@ def main() -> None:
         saved_stdout = os.dup(1)
         try:
             os.dup2(2, 1)
-            dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=device)
+            options = None
+            if args.nccl_priority == "high":
+                # NCCL's kernels on a high-priority stream: the block scheduler places their
+                # CTAs ahead of the prefill's pending ones
+                options = dist.ProcessGroupNCCL.Options(is_high_priority_stream=True)
+            dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=device, pg_options=options)
             dist.barrier(device_ids=[local])
             torch.cuda.synchronize()
         finally:
@@ -396,8 +409,13 @@ def main() -> None:
     from ab_attention_b200 import shard
 
     bh = shape.batch_heads
-    # tapered head blocks (largest first, one head per rank last) on N > 1
-    chunks = shard.taper_sizes(bh // world) if world > 1 else 1
+    # head blocks on N > 1: even (the default) or tapered (largest first, one head per rank last)
+    if world == 1:
+        chunks = 1
+    elif args.shard_blocks == "taper":
+        chunks = shard.taper_sizes(bh // world)
+    else:
+        chunks = [bh // world // shard.chunk_count(bh, world)] * shard.chunk_count(bh, world)
     heads = shard.rank_heads(bh, world, rank, chunks)
     per = len(heads)
     q, k, v, text = make_inputs(shape, device=device, bh_slice=heads if world > 1 else None)
@@ -423,7 +441,7 @@ def main() -> None:
             if e:
                 e[0].record(stream)
             shard.attention_sharded(qq, kk, vv, offsets, gathered, world=world, chunks=chunks,
-                                    sample_pages=shape.sample_pages, text_kv=text)
+                                    sample_pages=shape.sample_pages, text_kv=text, block_streams=args.block_streams)
             if e:
                 e[1].record(stream)
             return gathered
@@ -456,7 +474,8 @@ def main() -> None:
     if world > 1:
         # phases of one step measured separately (untimed for the headline): plan,
         # then prefill + overlapped all-gathers
-        phases = phase_times_sharded(shard, q, k, v, offsets, gathered, world, chunks, shape, text)
+        phases = phase_times_sharded(shard, q, k, v, offsets, gathered, world, chunks, shape, text,
+                                     block_streams=args.block_streams)
         plan_ms, prefill_ms = phases["plan_ms"], phases["prefill_and_gather_ms"]
     else:
         plan_ms = statistics.median(e[0].elapsed_time(e[1]) for e in ev)
