@@ -360,6 +360,8 @@ def main() -> None:
                         help="reference arm: skip timing the reference's own IBCS/SIP kernels on the GPU")
     parser.add_argument("--sample-pages", type=int, default=0,
                         help="override the configuration's sampled pages per row (the C4 sweep: 16..256)")
+    parser.add_argument("--sigma", type=float, default=0.0,
+                        help="override the configuration's Q/K frequency scale (the C4 sweep: 0.05, 0.1, 0.3)")
     parser.add_argument("--bh", type=int, default=0,
                         help="run only the first BH (batch*head) rows of the configuration (profiling)")
     args = parser.parse_args()
@@ -371,6 +373,10 @@ def main() -> None:
         import dataclasses
 
         shape = dataclasses.replace(shape, name=f"{shape.name}[p={args.sample_pages}]", sample_pages=args.sample_pages)
+    if args.sigma:
+        import dataclasses
+
+        shape = dataclasses.replace(shape, name=f"{shape.name}[sigma={args.sigma}]", sigma=args.sigma)
     if args.bh:
         import dataclasses
 
@@ -576,6 +582,7 @@ def main() -> None:
         "data": "synthetic smooth-field video tokens (seeded), random per-head projections",
         "config": {"workload": shape.name, "batch": shape.batch, "heads": shape.heads, "tokens": tokens,
                    "grid": [shape.frames, shape.height, shape.width], "sample_pages": shape.sample_pages,
+                   "sigma": shape.sigma, "cube_order": shape.cube,
                    "text_tokens": shape.text_tokens, "parallelism": f"heads{world}",
                    "l2": "inputs (Q/K/V 4.6 GB) larger than L2; no flush",
                    "step": "build_plan (fresh plan) + apply_plan"
