@@ -350,11 +350,15 @@ def cross_prefill(q3, k3, v3, *, ids=None, logw=None, samples=0, text_k=None, te
 # kernels only. A CPU tensor finds no kernel and raises, so there is no silent
 # fallback; C++ and TorchScript callers reach them without Python.
 
-def _load_torch_ops() -> None:
+def _load_torch_ops() -> bool:
+    """Registers the operators when libabx_torch.so is built. Before the build
+    (the build itself imports this package) they are simply absent, like every
+    kernel entry point, which raises until libabx.so exists."""
     path = _lib.PKG / "libabx_torch.so"
     if not path.exists():
-        raise ImportError(f"{path} is not built; run python -m ab_attention_b200.build")
+        return False
     torch.ops.load_library(str(path))
+    return True
 
 
-_load_torch_ops()
+TORCH_OPS_LOADED = _load_torch_ops()

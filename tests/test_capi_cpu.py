@@ -192,3 +192,12 @@ def test_torch_operators_are_cpp_with_meta_shapes():
     q3 = q.reshape(6, 1000, 128)
     o, lse = torch.ops.ab_attention.sparse_prefill(q3, q3, q3, ids, logw)
     assert o.shape == q3.shape and lse.shape == (6, 1000)
+
+
+def test_package_imports_before_the_operator_library_is_built(tmp_path, monkeypatch):
+    """The build runs as `python -m ab_attention_b200.build`, which imports the package
+    first: a checkout without libabx_torch.so must import (the operators are then absent)."""
+    from ab_attention_b200 import _lib, ops
+
+    monkeypatch.setattr(_lib, "PKG", tmp_path)
+    assert ops._load_torch_ops() is False
