@@ -59,6 +59,17 @@ int check_cuda(cudaError_t err, const char* what) {
     return fail(ABX_ERR_CUDA, "%s: %s", what, cudaGetErrorString(err));
 }
 
+// A driver API call reached through the runtime's entry-point table (no libcuda link).
+template <class Fn>
+Fn driver_entry(const char* name) {
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult status;
+    if (cudaGetDriverEntryPoint(name, &ptr, cudaEnableDefault, &status) != cudaSuccess ||
+        status != cudaDriverEntryPointSuccess)
+        return nullptr;
+    return reinterpret_cast<Fn>(ptr);
+}
+
 constexpr size_t kAlign = 256;
 size_t align_up(size_t x) { return (x + kAlign - 1) / kAlign * kAlign; }
 
@@ -299,19 +310,8 @@ namespace {
 constexpr size_t kStaticScratchBytes = size_t(256) << 20;
 static __device__ __align__(256) unsigned char g_static_scratch[kStaticScratchBytes];
 
-// Driver calls reached through the runtime's entry-point table (no libcuda link).
 using PfnCtxGetCurrent = CUresult (*)(CUcontext*);
 using PfnCtxGetId = CUresult (*)(CUcontext, unsigned long long*);
-
-template <class Fn>
-Fn driver_entry(const char* name) {
-    void* ptr = nullptr;
-    cudaDriverEntryPointQueryResult status;
-    if (cudaGetDriverEntryPoint(name, &ptr, cudaEnableDefault, &status) != cudaSuccess ||
-        status != cudaDriverEntryPointSuccess)
-        return nullptr;
-    return reinterpret_cast<Fn>(ptr);
-}
 
 // The array's device address per CUDA context, keyed by the context's unique
 // id (cuCtxGetId never reuses an id within a process). A host that creates its
@@ -478,6 +478,71 @@ int abx_sparse_prefill_paired(const void* q, const void* k, const void* v, int64
                                                static_cast<const abx::bf16*>(text_v), text_tokens,
                                                static_cast<abx::bf16*>(o), lse, workspace, workspace_bytes, stream),
                       "paired prefill launch");
+}
+
+int abx_ipc_handle(const void* ptr, void* handle, size_t* offset) {
+    if (ptr == nullptr || handle == nullptr || offset == nullptr)
+        return fail(ABX_ERR_INVALID_ARGUMENT, "ptr, handle and offset must be non-null");
+    using PfnAddressRange = CUresult (*)(CUdeviceptr*, size_t*, CUdeviceptr);
+    static const PfnAddressRange address_range = driver_entry<PfnAddressRange>("cuMemGetAddressRange");
+    if (address_range == nullptr) return fail(ABX_ERR_CUDA, "cuMemGetAddressRange unavailable in this driver");
+    CUdeviceptr base = 0;
+    size_t bytes = 0;
+    if (address_range(&base, &bytes, reinterpret_cast<CUdeviceptr>(ptr)) != CUDA_SUCCESS)
+        return fail(ABX_ERR_INVALID_ARGUMENT, "ptr is not device memory of this process");
+    cudaIpcMemHandle_t h;
+    if (int st = check_cuda(cudaIpcGetMemHandle(&h, reinterpret_cast<void*>(base)), "cudaIpcGetMemHandle")) return st;
+    std::memcpy(handle, &h, sizeof(h));
+    *offset = static_cast<size_t>(reinterpret_cast<CUdeviceptr>(ptr) - base);
+    return ABX_OK;
+}
+
+int abx_ipc_open(const void* handle, void** base) {
+    if (handle == nullptr || base == nullptr) return fail(ABX_ERR_INVALID_ARGUMENT, "handle and base must be non-null");
+    cudaIpcMemHandle_t h;
+    std::memcpy(&h, handle, sizeof(h));
+    return check_cuda(cudaIpcOpenMemHandle(base, h, cudaIpcMemLazyEnablePeerAccess), "cudaIpcOpenMemHandle");
+}
+
+int abx_ipc_close(void* base) {
+    if (base == nullptr) return fail(ABX_ERR_INVALID_ARGUMENT, "base must be non-null");
+    return check_cuda(cudaIpcCloseMemHandle(base), "cudaIpcCloseMemHandle");
+}
+
+int abx_sparse_prefill_scatter(const void* q, const void* k, const void* v, int64_t bh, int64_t seq,
+                               const int32_t* ids, const float* log_weights, int64_t samples, const void* text_k,
+                               const void* text_v, int64_t text_tokens, void* const* outs, int num_outs,
+                               int64_t out_head_base, int64_t out_heads, float* lse, void* workspace,
+                               size_t workspace_bytes, abx_stream_t stream) {
+    if (samples < 0 || text_tokens < 0)
+        return fail(ABX_ERR_INVALID_ARGUMENT, "negative sample or text token count");
+    if (outs == nullptr || num_outs < 1 || num_outs > abx::kMaxScatterOutputs)
+        return fail(ABX_ERR_INVALID_ARGUMENT, "between 1 and %d output buffers are needed (got %d)",
+                    abx::kMaxScatterOutputs, num_outs);
+    abx::bf16* dsts[abx::kMaxScatterOutputs];
+    for (int d = 0; d < num_outs; ++d) {
+        if (outs[d] == nullptr || !aligned16(outs[d]))
+            return fail(ABX_ERR_INVALID_ARGUMENT, "output buffer %d must be non-null and 16-byte aligned", d);
+        dsts[d] = static_cast<abx::bf16*>(outs[d]);
+    }
+    if (out_head_base < 0 || out_heads < out_head_base + bh)
+        return fail(ABX_ERR_INVALID_ARGUMENT, "heads [%lld, %lld) lie outside the %lld-head output",
+                    (long long)out_head_base, (long long)(out_head_base + bh), (long long)out_heads);
+    if (!abx::pair_supported(seq, samples, text_tokens))
+        return fail(ABX_ERR_UNSUPPORTED, "this shape cannot be paired (abx_prefill_workspace_size reports 0)");
+    if (int st = check_paired(q, k, v, bh, seq, ids, log_weights, samples, text_k, text_v, text_tokens, outs[0],
+                              workspace, workspace_bytes))
+        return st;
+    if (int st = check_cuda(abx::launch_pair_plan(ids, bh, seq, samples, text_tokens, workspace, workspace_bytes,
+                                                  stream),
+                            "pair plan launch"))
+        return st;
+    return check_cuda(abx::launch_pair_prefill(static_cast<const abx::bf16*>(q), static_cast<const abx::bf16*>(k),
+                                               static_cast<const abx::bf16*>(v), bh, seq, ids, log_weights, samples,
+                                               static_cast<const abx::bf16*>(text_k),
+                                               static_cast<const abx::bf16*>(text_v), text_tokens, nullptr, lse,
+                                               workspace, workspace_bytes, stream, dsts, num_outs, out_head_base),
+                      "scatter prefill launch");
 }
 
 int abx_pair_plan(const int32_t* ids, int64_t bh, int64_t seq, int64_t samples, int64_t text_tokens, void* workspace,

@@ -45,10 +45,14 @@ size_t pair_workspace_bytes(int64_t bh, int64_t seq, int64_t samples, int64_t te
 // calls needs its union lists built once.
 cudaError_t launch_pair_plan(const int32_t* ids, int64_t bh, int64_t seq, int64_t samples, int64_t text_tokens,
                              void* workspace, size_t workspace_bytes, cudaStream_t stream);
+// outs / num_outs (up to kMaxScatterOutputs): write every output row to each of
+// these [heads, seq, 128] buffers at head out_head_base + head instead of to o.
+constexpr int kMaxScatterOutputs = 8;
 cudaError_t launch_pair_prefill(const bf16* q, const bf16* k, const bf16* v, int64_t bh, int64_t seq,
                                 const int32_t* ids, const float* log_weights, int64_t samples, const bf16* text_k,
                                 const bf16* text_v, int64_t text_tokens, bf16* o, float* lse, void* workspace,
-                                size_t workspace_bytes, cudaStream_t stream);
+                                size_t workspace_bytes, cudaStream_t stream, bf16* const* outs = nullptr,
+                                int num_outs = 0, int64_t out_head_base = 0);
 cudaError_t launch_prefill_pair(const bf16* q, const bf16* k, const bf16* v, int64_t bh, int64_t seq,
                                 const int32_t* ids, const float* log_weights, int64_t samples, const bf16* text_k,
                                 const bf16* text_v, int64_t text_tokens, bf16* o, float* lse, void* workspace,

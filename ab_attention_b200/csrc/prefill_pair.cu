@@ -321,6 +321,12 @@ struct PairArgs {
     int text_tail;
     float kappa;
     int* error;
+    // Scatter form (num_outs > 0): every output row goes to each of `outs`, buffers
+    // of the whole layer's [heads, seq, 128] output (on this GPU or on peers,
+    // through their mapped addresses), at head out_head_base + head; `o` is unused.
+    bf16* outs[kMaxScatterOutputs];
+    int num_outs;
+    int64_t out_head_base;
 };
 
 struct PairMaps {
@@ -713,10 +719,22 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_pair_kernel(const PairArg
                     pw[e] = *reinterpret_cast<uint32_t*>(&pair);
                 }
                 if (r < n) {
-                    reinterpret_cast<uint4*>(out_row + kChunk * c)[0] = packed[0];
-                    reinterpret_cast<uint4*>(out_row + kChunk * c)[1] = packed[1];
+                    if (args.num_outs == 0) {
+                        reinterpret_cast<uint4*>(out_row + kChunk * c)[0] = packed[0];
+                        reinterpret_cast<uint4*>(out_row + kChunk * c)[1] = packed[1];
+                    } else {
+                        const int64_t row_off = ((args.out_head_base + head) * args.seq + token0 + r) * kHeadDim;
+                        for (int d = 0; d < args.num_outs; ++d) {
+                            uint4* dst = reinterpret_cast<uint4*>(args.outs[d] + row_off + kChunk * c);
+                            dst[0] = packed[0];
+                            dst[1] = packed[1];
+                        }
+                    }
                 }
             }
+            // Peers read the scattered rows once they learn (through a later
+            // collective) that this kernel finished: make them visible system-wide.
+            if (args.num_outs > 0) __threadfence_system();
             if (args.lse != nullptr && r < n) args.lse[head * args.seq + token0 + r] = m_used + log2f(l_sum);
         }
     }
@@ -806,8 +824,10 @@ cudaError_t launch_pair_plan(const int32_t* ids, int64_t bh, int64_t seq, int64_
 cudaError_t launch_pair_prefill(const bf16* q, const bf16* k, const bf16* v, int64_t bh, int64_t seq,
                                 const int32_t* ids, const float* log_weights, int64_t samples, const bf16* text_k,
                                 const bf16* text_v, int64_t text_tokens, bf16* o, float* lse, void* workspace,
-                                size_t workspace_bytes, cudaStream_t stream) {
+                                size_t workspace_bytes, cudaStream_t stream, bf16* const* outs, int num_outs,
+                                int64_t out_head_base) {
     if (workspace_bytes < pair_workspace_bytes(bh, seq, samples, text_tokens)) return cudaErrorInvalidValue;
+    if (num_outs < 0 || num_outs > kMaxScatterOutputs || (num_outs > 0 && outs == nullptr)) return cudaErrorInvalidValue;
     const PairLayout l = pair_layout(bh, seq, samples, text_tokens, workspace);
     PairArgs args{};
     args.ids = ids;
@@ -828,6 +848,9 @@ cudaError_t launch_pair_prefill(const bf16* q, const bf16* k, const bf16* v, int
     args.text_tail = static_cast<int>(text_tokens % kKv4);
     args.kappa = qk_scale_log2();
     args.error = device_error_word();
+    args.num_outs = num_outs;
+    args.out_head_base = out_head_base;
+    for (int d = 0; d < num_outs; ++d) args.outs[d] = outs[d];
     PairMaps maps;
     cudaError_t err;
     if ((err = encode_rows(&maps.q, q, bh * seq, 128)) != cudaSuccess) return err;

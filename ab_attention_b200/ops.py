@@ -308,6 +308,30 @@ def sparse_prefill_planned(q3, k3, v3, ids, logw, workspace, *, text_k=None, tex
     return o, lse_
 
 
+def sparse_prefill_scatter(q3, k3, v3, ids, logw, outs, *, head_base: int, out_heads: int, text_k=None,
+                           text_v=None, return_lse=False):
+    """The paired prefill of [BH,S,128] q/k/v writing its rows straight into each
+    buffer of `outs` (device addresses, ints, of [out_heads, S, 128] bf16 layer
+    outputs, on this GPU or mapped from peers) at heads [head_base, head_base + BH).
+    Returns the base-2 LSE of these heads (or None)."""
+    _check_attention_inputs(q3, k3, v3, ids, logw, text_k, text_v)
+    bh, seq, _ = q3.shape
+    samples = ids.shape[-1]
+    text_tokens = 0 if text_k is None else text_k.shape[1]
+    lse_ = torch.empty((bh, seq), dtype=torch.float32, device=q3.device) if return_lse else None
+    ws = prefill_workspace(bh, seq, samples, text_tokens, q3.device)
+    if ws is None:
+        raise RuntimeError("this shape cannot take the paired prefill, so it cannot scatter")
+    ptrs = (ctypes.c_void_p * len(outs))(*[int(p) for p in outs])
+    lib = _lib.load()
+    with torch.cuda.device(q3.device):
+        _lib.check(lib.abx_sparse_prefill_scatter(
+            _lib.ptr(q3), _lib.ptr(k3), _lib.ptr(v3), bh, seq, _lib.ptr(ids), _lib.ptr(logw), samples,
+            _lib.ptr(text_k), _lib.ptr(text_v), text_tokens, ptrs, len(outs), head_base, out_heads, _lib.ptr(lse_),
+            _lib.ptr(ws), ws.numel(), _lib.stream_of(q3)), "abx_sparse_prefill_scatter")
+    return lse_
+
+
 def dense_prefill(q3, k3, v3, *, return_lse=False):
     """Dense attention through the same prefill kernel (the dense comparator)."""
     _check_attention_inputs(q3, k3, v3)

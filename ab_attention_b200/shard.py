@@ -281,3 +281,106 @@ def attention_sharded_host(q, k, v, offsets, out, host_out, *, world: int, chunk
             work.wait()
     main.wait_stream(copy_out)
     return out
+
+
+# ---- output scatter over peer memory --------------------------------------------------------
+
+class PeerOutputs:
+    """Every rank's [BH, S, 128] layer output, mapped into this process.
+
+    Each rank allocates its own copy of the layer output; the ranks exchange CUDA
+    IPC handles (abx_ipc_handle) over the process group and map the others'
+    copies for this rank's device (abx_ipc_open, peer access enabled), so one
+    kernel can store its rows into all of them over NVLink. `pointers` lists the
+    device addresses in rank order (this rank's own copy at its rank). Call
+    `close()` before the process group is destroyed.
+    """
+
+    def __init__(self, out: torch.Tensor, group=None):
+        import ctypes
+
+        import torch.distributed as dist
+
+        from . import _lib
+
+        self.out = out
+        self._lib = _lib.load()
+        world = dist.get_world_size(group)
+        rank = dist.get_rank(group)
+        handle = ctypes.create_string_buffer(64)
+        offset = ctypes.c_size_t(0)
+        with torch.cuda.device(out.device):
+            _lib.check(self._lib.abx_ipc_handle(_lib.ptr(out), handle, ctypes.byref(offset)), "abx_ipc_handle")
+        shared = [None] * world
+        dist.all_gather_object(shared, (bytes(handle.raw), offset.value), group=group)
+        self._opened = []
+        self.pointers = []
+        with torch.cuda.device(out.device):
+            for r, (raw, off) in enumerate(shared):
+                if r == rank:
+                    self.pointers.append(out.data_ptr())
+                    continue
+                base = ctypes.c_void_p(0)
+                _lib.check(self._lib.abx_ipc_open(ctypes.create_string_buffer(raw, 64), ctypes.byref(base)),
+                           "abx_ipc_open")
+                self._opened.append(base.value)
+                self.pointers.append(base.value + off)
+
+    def close(self) -> None:
+        import ctypes
+
+        from . import _lib
+
+        with torch.cuda.device(self.out.device):
+            for base in self._opened:
+                _lib.check(self._lib.abx_ipc_close(ctypes.c_void_p(base)), "abx_ipc_close")
+        self._opened = []
+        self.pointers = []
+
+
+def attention_scatter(q, k, v, offsets, peers: PeerOutputs, *, rank: int, world: int, sample_pages: int = 64,
+                      text_kv=None, group=None, timing: dict | None = None):
+    """This rank's part of a head-sharded AB-attention layer whose output needs no
+    all-gather: the rank plans its contiguous heads (`head_slice(BH, world,
+    rank)`), and one paired-prefill launch writes every output row into all
+    ranks' copies of the layer output (`peers`) through peer stores over NVLink.
+
+    Two one-element all-reduces on the current stream bracket the launch: the
+    first orders it after every rank's earlier readers of the output (the
+    buffers are overwritten), the second tells every rank that all rows have
+    landed. Returns when `peers.out` is complete on the current stream.
+    """
+    import torch.distributed as dist
+
+    from . import ops
+    from .attention import build_plan
+
+    per, tokens, dim = q.shape[1], q.shape[2], q.shape[3]
+    bh = per * world
+    flag = torch.zeros(1, dtype=torch.float32, device=q.device)
+
+    def event():
+        e = torch.cuda.Event(enable_timing=True)
+        e.record()
+        return e
+
+    dist.all_reduce(flag, group=group)
+    start = event() if timing is not None else None
+    plan = build_plan(q, k, sample_pages=sample_pages, offsets=offsets)
+    planned = event() if timing is not None else None
+    rows = plan.descriptor.shape[0]
+    ids = plan.descriptor.reshape(rows, -1).contiguous()
+    logw = plan.log_weights.reshape(rows, -1).contiguous()
+    tk = tv = None
+    if text_kv is not None:
+        tk, tv = (t.reshape(per, -1, dim).contiguous() for t in text_kv)
+    ops.sparse_prefill_scatter(q.reshape(per, tokens, dim).contiguous(), k.reshape(per, tokens, dim).contiguous(),
+                               v.reshape(per, tokens, dim).contiguous(), ids, logw, peers.pointers,
+                               head_base=rank * per, out_heads=bh, text_k=tk, text_v=tv)
+    attended = event() if timing is not None else None
+    dist.all_reduce(flag, group=group)
+    if timing is not None:
+        timing["plan"] = (start, planned)
+        timing["blocks"] = [(planned, attended)]
+        timing["tail"] = (attended, event())
+    return peers.out

@@ -277,20 +277,17 @@ def run_reference(args, shape) -> None:
 
 # ---- GPU arm -----------------------------------------------------------------------
 
-def phase_times_sharded(shard, q, k, v, offsets, gathered, world, chunks, shape, text, reps=3,
-                        block_streams: int = 1) -> dict:
-    """Phases of a sharded step from events inside attention_sharded (median of
-    `reps` untimed steps): the plan, each head block's prefill, and the
-    all-gather time left exposed after the last block's prefill."""
+def phase_times_sharded(step, chunks, reps=3) -> dict:
+    """Phases of a sharded step from events inside it (median of `reps` untimed
+    steps): the plan, each head block's prefill, and the output reassembly left
+    exposed after the last block's prefill. `step(timing)` runs one step."""
     import torch.distributed as dist
 
     samples = []
     for _ in range(reps):
         dist.barrier()
         timing = {}
-        shard.attention_sharded(q, k, v, offsets, gathered, world=world, chunks=chunks,
-                                sample_pages=shape.sample_pages, text_kv=text, timing=timing,
-                                block_streams=block_streams)
+        step(timing)
         torch.cuda.synchronize()
         samples.append(timing)
     med = statistics.median
@@ -354,6 +351,9 @@ def main() -> None:
                         help="N > 1: head blocks of equal size, or tapered to one head per rank last")
     parser.add_argument("--block-streams", type=int, default=1,
                         help="N > 1: streams the head blocks' prefills alternate between")
+    parser.add_argument("--gather", default="nccl", choices=["nccl", "peer"],
+                        help="N > 1: reassemble the output with NCCL all-gathers of head blocks, or have the "
+                             "prefill store every row into all ranks' copies over NVLink (peer)")
     parser.add_argument("--nccl-priority", default="normal", choices=["normal", "high"],
                         help="N > 1: priority of NCCL's stream")
     parser.add_argument("--no-ref-kernels", action="store_true",
@@ -416,7 +416,7 @@ def main() -> None:
 
     bh = shape.batch_heads
     # head blocks on N > 1: even (the default) or tapered (largest first, one head per rank last)
-    if world == 1:
+    if world == 1 or args.gather == "peer":
         chunks = 1
     elif args.shard_blocks == "taper":
         chunks = shard.taper_sizes(bh // world)
@@ -431,6 +431,15 @@ def main() -> None:
     tokens = shape.tokens
     offsets = shard.shard_offsets(shard.layer_offsets(bh, tokens, shape.seed, device), tokens, heads)
     gathered = torch.empty((bh, tokens, 128), dtype=torch.bfloat16, device=device) if world > 1 else None
+    peers = shard.PeerOutputs(gathered) if world > 1 and args.gather == "peer" else None
+
+    def sharded_step(qq, kk, vv, timing=None):
+        if peers is not None:
+            return shard.attention_scatter(qq, kk, vv, offsets, peers, rank=rank, world=world,
+                                           sample_pages=shape.sample_pages, text_kv=text, timing=timing)
+        return shard.attention_sharded(qq, kk, vv, offsets, gathered, world=world, chunks=chunks,
+                                       sample_pages=shape.sample_pages, text_kv=text, timing=timing,
+                                       block_streams=args.block_streams)
 
     def barrier():
         if world > 1:
@@ -446,8 +455,7 @@ def main() -> None:
             # all-gather overlapping the next block's prefill
             if e:
                 e[0].record(stream)
-            shard.attention_sharded(qq, kk, vv, offsets, gathered, world=world, chunks=chunks,
-                                    sample_pages=shape.sample_pages, text_kv=text, block_streams=args.block_streams)
+            sharded_step(qq, kk, vv)
             if e:
                 e[1].record(stream)
             return gathered
@@ -480,8 +488,7 @@ def main() -> None:
     if world > 1:
         # phases of one step measured separately (untimed for the headline): plan,
         # then prefill + overlapped all-gathers
-        phases = phase_times_sharded(shard, q, k, v, offsets, gathered, world, chunks, shape, text,
-                                     block_streams=args.block_streams)
+        phases = phase_times_sharded(lambda timing: sharded_step(q, k, v, timing), chunks)
         plan_ms, prefill_ms = phases["plan_ms"], phases["prefill_and_gather_ms"]
     else:
         plan_ms = statistics.median(e[0].elapsed_time(e[1]) for e in ev)
@@ -501,7 +508,8 @@ def main() -> None:
         tb = torch.tensor([phases["exposed_gather_ms"], *phases["prefill_ms_per_block"]], device=device)
         dist.all_reduce(tb, op=dist.ReduceOp.MAX)
         values = tb.tolist()
-        sharded = {"head_blocks": chunks, "heads_per_rank": per, "exposed_gather_ms": values[0],
+        sharded = {"output": "peer stores from the prefill" if peers is not None else "NCCL all-gather per block",
+                   "head_blocks": chunks, "heads_per_rank": per, "exposed_gather_ms": values[0],
                    "prefill_ms_per_block": values[1:],
                    "note": "events inside attention_sharded on an untimed step, max over ranks; the exposed "
                            "gather is the wait for the last block's all-gather after its prefill"}
@@ -627,6 +635,10 @@ def main() -> None:
         print(json.dumps(line), flush=True)
     if world > 1:
         dist.barrier()
+        if peers is not None:
+            torch.cuda.synchronize()
+            dist.barrier()
+            peers.close()
         dist.destroy_process_group()
 
 

@@ -171,6 +171,33 @@ int abx_sparse_prefill_paired_planned(const void* q, const void* k, const void* 
                                       const void* text_k, const void* text_v, int64_t text_tokens, void* o,
                                       float* lse, void* workspace, size_t workspace_bytes, abx_stream_t stream);
 
+/* CUDA IPC of an output buffer between the processes of one node (no
+ * counterpart in the reference): abx_ipc_handle gives the 64-byte handle of the
+ * allocation holding `ptr` and ptr's byte offset in it; another process opens
+ * it with abx_ipc_open (the mapping is made for the caller's current device,
+ * with peer access enabled to the owner's device) and adds the offset, then
+ * closes it with abx_ipc_close. */
+int abx_ipc_handle(const void* ptr, void* handle, size_t* offset);
+int abx_ipc_open(const void* handle, void** base);
+int abx_ipc_close(void* base);
+
+/* The paired prefill (pair plan included) with its output rows written straight
+ * into `num_outs` (1..8) copies of the whole layer's output, each [out_heads,
+ * seq, 128] bf16, at heads [out_head_base, out_head_base + bh): on several GPUs,
+ * one copy per rank, the other ranks' reached through their mapped (CUDA IPC)
+ * addresses, so a head-sharded layer needs no all-gather afterwards. No
+ * counterpart in the reference (it has no multi-GPU path); it replaces the NCCL
+ * all-gather of the sharded outputs. The stores are plain peer stores over
+ * NVLink, made visible system-wide before the kernel ends; the caller orders a
+ * reader on another GPU after this call with any collective (an all-reduce of
+ * one element) issued on `stream` after it. lse (optional) is this call's heads
+ * only, [bh, seq]. ABX_ERR_UNSUPPORTED for a shape that cannot be paired. */
+int abx_sparse_prefill_scatter(const void* q, const void* k, const void* v, int64_t bh, int64_t seq,
+                               const int32_t* ids, const float* log_weights, int64_t samples,
+                               const void* text_k, const void* text_v, int64_t text_tokens,
+                               void* const* outs, int num_outs, int64_t out_head_base, int64_t out_heads,
+                               float* lse, void* workspace, size_t workspace_bytes, abx_stream_t stream);
+
 /* Dense attention through the same prefill kernel (every KV4 block, shift 0):
  * the dense comparator. o / lse as above. */
 int abx_dense_prefill(const void* q, const void* k, const void* v, int64_t bh, int64_t seq,

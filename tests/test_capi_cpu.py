@@ -201,3 +201,23 @@ def test_package_imports_before_the_operator_library_is_built(tmp_path, monkeypa
 
     monkeypatch.setattr(_lib, "PKG", tmp_path)
     assert ops._load_torch_ops() is False
+
+
+def test_scatter_prefill_validates_outputs_before_launch():
+    import ctypes
+
+    lib = _lib.load()
+    p = ctypes.c_void_p(16)
+    one = (ctypes.c_void_p * 1)(16)
+    # no output buffers; a null one; heads past the output; negative counts
+    assert lib.abx_sparse_prefill_scatter(p, p, p, 2, 1024, p, p, 8, None, None, 0, one, 0, 0, 2, None, p,
+                                          1 << 30, None) == 1
+    assert lib.abx_sparse_prefill_scatter(p, p, p, 2, 1024, p, p, 8, None, None, 0, (ctypes.c_void_p * 1)(0), 1,
+                                          0, 2, None, p, 1 << 30, None) == 1
+    assert lib.abx_sparse_prefill_scatter(p, p, p, 2, 1024, p, p, 8, None, None, 0, one, 1, 3, 4, None, p,
+                                          1 << 30, None) == 1
+    assert lib.abx_sparse_prefill_scatter(p, p, p, 2, 1024, p, p, -8, None, None, 0, one, 1, 0, 2, None, p,
+                                          1 << 30, None) == 1
+    # IPC entry points refuse null arguments without touching the driver
+    assert lib.abx_ipc_handle(None, None, None) == 1
+    assert lib.abx_ipc_open(None, None) == 1

@@ -181,3 +181,24 @@ def test_paired_matches_unpaired_at_full_size(config, heads):
     diff = (o1.float() - o0.float()).abs()
     assert diff.max().item() <= MAX_ERR and diff.mean().item() <= MEAN_ERR / 4, (diff.max().item(), diff.mean().item())
     assert (l1 - l0).abs().max().item() <= LSE_ERR
+
+
+def test_scatter_writes_every_row_into_every_output():
+    """abx_sparse_prefill_scatter stores each row of its heads into every output
+    buffer at the given head offset, bit-identical to the paired prefill, and
+    touches no other head."""
+    bh, grid = 3, (2, 16, 40)
+    q, k, v = _fields(bh, grid, seed=16)
+    plan = build_plan(q.unsqueeze(0), k.unsqueeze(0), sample_pages=2, seed=6)
+    rows = plan.descriptor.shape[0]
+    ids = plan.descriptor.reshape(rows, -1).contiguous()
+    logw = plan.log_weights.reshape(rows, -1).contiguous()
+    want, want_lse = ops.sparse_prefill(q, k, v, ids, logw, return_lse=True, paired=True)
+    outs = [torch.full((5, q.shape[1], 128), 7.0, dtype=torch.bfloat16, device="cuda") for _ in range(2)]
+    lse = ops.sparse_prefill_scatter(q, k, v, ids, logw, [o.data_ptr() for o in outs], head_base=1, out_heads=5,
+                                     return_lse=True)
+    torch.cuda.synchronize()
+    for o in outs:
+        assert torch.equal(o[1:4], want)
+        assert bool((o[0] == 7.0).all()) and bool((o[4] == 7.0).all())
+    assert torch.equal(lse, want_lse)
