@@ -121,9 +121,10 @@ class ClockSampler:
 
 
 # DRAM bytes (read + write) of one paired prefill launch per head at the Wan shape,
-# from one ncu capture of the 2-head case (dram__bytes_read.sum + dram__bytes_write.sum
-# = 138.85 + 21.98 MB); a head's K/V stay L2-resident, so traffic scales with heads.
-PREFILL_DRAM_BYTES_PER_HEAD = (138.85e6 + 21.98e6) / 2
+# from one ncu capture of the 4-head case (dram__bytes_read.sum + dram__bytes_write.sum
+# = 279.82 + 63.76 MB; its 232 MB of Q/K/V exceed L2); a head's K/V stay L2-resident
+# while its pairs run, so traffic scales with heads.
+PREFILL_DRAM_BYTES_PER_HEAD = (279.82e6 + 63.76e6) / 4
 
 
 def plan_bytes(bh: int, tokens: int, samples: int) -> float:
