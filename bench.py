@@ -595,8 +595,11 @@ def main() -> None:
                    "text_tokens": shape.text_tokens, "parallelism": f"heads{world}",
                    "l2": "inputs (Q/K/V 4.6 GB) larger than L2; no flush",
                    "step": "build_plan (fresh plan) + apply_plan"
-                           + (f" in head blocks of {chunks} heads per rank, each all-gathered while the next "
-                              f"computes" if world > 1 else "")},
+                           + ("" if world == 1 else
+                              " with every output row stored into all ranks' copies by the prefill (peer stores)"
+                              if args.gather == "peer" else
+                              f" in head blocks of {chunks} heads per rank, each all-gathered while the next "
+                              f"computes")},
         "eff_tflops": eq_flops / (ms * 1e-3) / 1e12,
         "sparse_tflops": sparse_flops / (ms * 1e-3) / 1e12,
         "plan_ms": plan_ms, "prefill_ms": prefill_ms,
@@ -620,7 +623,7 @@ def main() -> None:
                                   "fast-math exp2/log2/division work and the double-precision SIP sums"},
         # cluster, pool, lse, sip + a pair plan and a prefill per head block per step
         # (NCCL's kernels not counted)
-        "gpu_launches": (3 + 2 * (len(chunks) if world > 1 else 1)) * args.steps,
+        "gpu_launches": (3 + 2 * (len(chunks) if isinstance(chunks, list) else 1)) * args.steps,
         "clocks": clocks.summary(),
         **dense,
     }
