@@ -44,6 +44,7 @@ _SIGNATURES = {
     "abx_ipc_handle": ([_p, _p, ctypes.POINTER(ctypes.c_size_t)], ctypes.c_int),
     "abx_ipc_open": ([_p, ctypes.POINTER(ctypes.c_void_p)], ctypes.c_int),
     "abx_ipc_close": ([_p], ctypes.c_int),
+    "abx_peer_copy": ([_p, _p, ctypes.c_size_t, _p], ctypes.c_int),
     "abx_sparse_prefill_scatter": ([_p, _p, _p, _i64, _i64, _p, _p, _i64, _p, _p, _i64, _p, ctypes.c_int, _i64,
                                     _i64, _p, _p, ctypes.c_size_t, _p], ctypes.c_int),
     "abx_dense_prefill": ([_p, _p, _p, _i64, _i64, _p, _p, _p], ctypes.c_int),

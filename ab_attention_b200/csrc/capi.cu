@@ -509,6 +509,12 @@ int abx_ipc_close(void* base) {
     return check_cuda(cudaIpcCloseMemHandle(base), "cudaIpcCloseMemHandle");
 }
 
+int abx_peer_copy(void* dst, const void* src, size_t bytes, abx_stream_t stream) {
+    if (dst == nullptr || src == nullptr) return fail(ABX_ERR_INVALID_ARGUMENT, "dst and src must be non-null");
+    if (bytes == 0) return ABX_OK;
+    return check_cuda(cudaMemcpyAsync(dst, src, bytes, cudaMemcpyDefault, stream), "peer copy");
+}
+
 int abx_sparse_prefill_scatter(const void* q, const void* k, const void* v, int64_t bh, int64_t seq,
                                const int32_t* ids, const float* log_weights, int64_t samples, const void* text_k,
                                const void* text_v, int64_t text_tokens, void* const* outs, int num_outs,

@@ -305,6 +305,7 @@ class PeerOutputs:
 
         self.out = out
         self._lib = _lib.load()
+        self.copy_stream = torch.cuda.Stream(out.device)  # peer copies of finished head blocks
         world = dist.get_world_size(group)
         rank = dist.get_rank(group)
         handle = ctypes.create_string_buffer(64)
@@ -384,3 +385,82 @@ def attention_scatter(q, k, v, offsets, peers: PeerOutputs, *, rank: int, world:
         timing["blocks"] = [(planned, attended)]
         timing["tail"] = (attended, event())
     return peers.out
+
+
+def attention_copied(q, k, v, offsets, peers: PeerOutputs, *, rank: int, world: int, chunks, sample_pages: int = 64,
+                     text_kv=None, group=None, timing: dict | None = None):
+    """`attention_sharded` with the all-gather done by copy engines.
+
+    Same block-interleaved heads and plan as `attention_sharded`; each block's
+    prefill writes its rows straight into this rank's copy of the layer output
+    (at the block's global heads), and as soon as it finishes, a copy stream
+    pushes that slice into every other rank's copy (`abx_peer_copy` through the
+    `peers` mappings: copy engines over NVLink, no SMs), so the next block's
+    prefill keeps every SM. Two one-element all-reduces bracket the step, as in
+    `attention_scatter`. Returns when `peers.out` is complete on the current stream.
+    """
+    import torch.distributed as dist
+
+    from . import _lib, ops
+    from .attention import build_plan
+
+    per, tokens, dim = q.shape[1], q.shape[2], q.shape[3]
+    sizes = block_sizes(per * world, world, chunks)
+    bh = per * world
+    qb = math.ceil(tokens / 128)
+    head_bytes = tokens * dim * q.element_size()
+    lib = _lib.load()
+    main = torch.cuda.current_stream(q.device)
+    copy = peers.copy_stream
+    own = peers.pointers[rank]
+    flag = torch.zeros(1, dtype=torch.float32, device=q.device)
+
+    def event():
+        e = torch.cuda.Event(enable_timing=True)
+        e.record(main)
+        return e
+
+    dist.all_reduce(flag, group=group)  # every rank is done with the buffers this step overwrites
+    if timing is not None:
+        timing["blocks"] = []
+        plan_start = event()
+    plan = build_plan(q, k, sample_pages=sample_pages, offsets=offsets)
+    if timing is not None:
+        timing["plan"] = (plan_start, event())
+    rows_all = plan.descriptor.shape[0]
+    ids = plan.descriptor.reshape(rows_all, -1).contiguous()
+    logw = plan.log_weights.reshape(rows_all, -1).contiguous()
+    q3, k3, v3 = (x.reshape(per, tokens, dim) for x in (q, k, v))
+    text3 = None if text_kv is None else tuple(t.reshape(per, -1, dim) for t in text_kv)
+    first = local = 0
+    for b in sizes:
+        heads = slice(local, local + b)
+        rows = slice(local * qb, (local + b) * qb)
+        head0 = first + rank * b  # this rank's first head of the block, in the layer's order
+        start = event() if timing is not None else None
+        ops.sparse_prefill_scatter(q3[heads], k3[heads], v3[heads], ids[rows], logw[rows], [own], head_base=head0,
+                                   out_heads=bh, text_k=None if text3 is None else text3[0][heads],
+                                   text_v=None if text3 is None else text3[1][heads])
+        done = event()
+        if timing is not None:
+            timing["blocks"].append((start, done))
+        copy.wait_event(done)
+        for r, ptr in enumerate(peers.pointers):
+            if r != rank:
+                _lib.check(lib.abx_peer_copy(ctypes_void_p(ptr + head0 * head_bytes),
+                                             ctypes_void_p(own + head0 * head_bytes), b * head_bytes,
+                                             ctypes_void_p(copy.cuda_stream)), "abx_peer_copy")
+        first += world * b
+        local += b
+    tail_start = event() if timing is not None else None
+    main.wait_stream(copy)
+    dist.all_reduce(flag, group=group)  # every rank's rows have landed in every copy
+    if timing is not None:
+        timing["tail"] = (tail_start, event())
+    return peers.out
+
+
+def ctypes_void_p(value: int):
+    import ctypes
+
+    return ctypes.c_void_p(value)

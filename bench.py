@@ -352,9 +352,10 @@ def main() -> None:
                         help="N > 1: head blocks of equal size, or tapered to one head per rank last")
     parser.add_argument("--block-streams", type=int, default=1,
                         help="N > 1: streams the head blocks' prefills alternate between")
-    parser.add_argument("--gather", default="nccl", choices=["nccl", "peer"],
-                        help="N > 1: reassemble the output with NCCL all-gathers of head blocks, or have the "
-                             "prefill store every row into all ranks' copies over NVLink (peer)")
+    parser.add_argument("--gather", default="nccl", choices=["nccl", "copy", "peer"],
+                        help="N > 1: reassemble the output with NCCL all-gathers of head blocks, with copy-engine "
+                             "peer copies of each finished block (copy), or have the prefill store every row "
+                             "into all ranks' copies over NVLink (peer)")
     parser.add_argument("--nccl-priority", default="normal", choices=["normal", "high"],
                         help="N > 1: priority of NCCL's stream")
     parser.add_argument("--no-ref-kernels", action="store_true",
@@ -432,9 +433,12 @@ def main() -> None:
     tokens = shape.tokens
     offsets = shard.shard_offsets(shard.layer_offsets(bh, tokens, shape.seed, device), tokens, heads)
     gathered = torch.empty((bh, tokens, 128), dtype=torch.bfloat16, device=device) if world > 1 else None
-    peers = shard.PeerOutputs(gathered) if world > 1 and args.gather == "peer" else None
+    peers = shard.PeerOutputs(gathered) if world > 1 and args.gather in ("peer", "copy") else None
 
     def sharded_step(qq, kk, vv, timing=None):
+        if args.gather == "copy":
+            return shard.attention_copied(qq, kk, vv, offsets, peers, rank=rank, world=world, chunks=chunks,
+                                          sample_pages=shape.sample_pages, text_kv=text, timing=timing)
         if peers is not None:
             return shard.attention_scatter(qq, kk, vv, offsets, peers, rank=rank, world=world,
                                            sample_pages=shape.sample_pages, text_kv=text, timing=timing)
@@ -509,7 +513,8 @@ def main() -> None:
         tb = torch.tensor([phases["exposed_gather_ms"], *phases["prefill_ms_per_block"]], device=device)
         dist.all_reduce(tb, op=dist.ReduceOp.MAX)
         values = tb.tolist()
-        sharded = {"output": "peer stores from the prefill" if peers is not None else "NCCL all-gather per block",
+        sharded = {"output": {"nccl": "NCCL all-gather per block", "copy": "copy-engine peer copies per block",
+                              "peer": "peer stores from the prefill"}[args.gather],
                    "head_blocks": chunks, "heads_per_rank": per, "exposed_gather_ms": values[0],
                    "prefill_ms_per_block": values[1:],
                    "note": "events inside attention_sharded on an untimed step, max over ranks; the exposed "
@@ -598,6 +603,8 @@ def main() -> None:
                            + ("" if world == 1 else
                               " with every output row stored into all ranks' copies by the prefill (peer stores)"
                               if args.gather == "peer" else
+                              f" in head blocks of {chunks} heads per rank, each copied to every rank by copy "
+                              f"engines while the next computes" if args.gather == "copy" else
                               f" in head blocks of {chunks} heads per rank, each all-gathered while the next "
                               f"computes")},
         "eff_tflops": eq_flops / (ms * 1e-3) / 1e12,

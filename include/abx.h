@@ -181,6 +181,11 @@ int abx_ipc_handle(const void* ptr, void* handle, size_t* offset);
 int abx_ipc_open(const void* handle, void** base);
 int abx_ipc_close(void* base);
 
+/* Asynchronous copy of `bytes` on `stream`, either address possibly another
+ * GPU's (a mapping opened by abx_ipc_open): between GPUs it runs on a copy
+ * engine over NVLink and uses no SMs. No counterpart in the reference. */
+int abx_peer_copy(void* dst, const void* src, size_t bytes, abx_stream_t stream);
+
 /* The paired prefill (pair plan included) with its output rows written straight
  * into `num_outs` (1..8) copies of the whole layer's output, each [out_heads,
  * seq, 128] bf16, at heads [out_head_base, out_head_base + bh): on several GPUs,
