@@ -20,9 +20,15 @@ computes. Consecutive blocks' prefills can also alternate between streams
 last wave leaves idle; measured on 8 B200s this starves NCCL's all-gather
 kernels of SMs (the gathers then queue behind the prefills), so one stream is
 the default.
+
+Two alternatives to the NCCL all-gather share every rank's copy of the output
+through CUDA IPC (`PeerOutputs`): `attention_copied` pushes each finished head
+block to the other ranks with copy engines, and `attention_scatter` has the
+prefill store every output row into all copies itself.
 """
 from __future__ import annotations
 
+import ctypes
 import math
 
 import torch
@@ -297,8 +303,6 @@ class PeerOutputs:
     """
 
     def __init__(self, out: torch.Tensor, group=None):
-        import ctypes
-
         import torch.distributed as dist
 
         from . import _lib
@@ -328,8 +332,6 @@ class PeerOutputs:
                 self.pointers.append(base.value + off)
 
     def close(self) -> None:
-        import ctypes
-
         from . import _lib
 
         with torch.cuda.device(self.out.device):
@@ -447,9 +449,9 @@ def attention_copied(q, k, v, offsets, peers: PeerOutputs, *, rank: int, world: 
         copy.wait_event(done)
         for r, ptr in enumerate(peers.pointers):
             if r != rank:
-                _lib.check(lib.abx_peer_copy(ctypes_void_p(ptr + head0 * head_bytes),
-                                             ctypes_void_p(own + head0 * head_bytes), b * head_bytes,
-                                             ctypes_void_p(copy.cuda_stream)), "abx_peer_copy")
+                _lib.check(lib.abx_peer_copy(ctypes.c_void_p(ptr + head0 * head_bytes),
+                                             ctypes.c_void_p(own + head0 * head_bytes), b * head_bytes,
+                                             ctypes.c_void_p(copy.cuda_stream)), "abx_peer_copy")
         first += world * b
         local += b
     tail_start = event() if timing is not None else None
@@ -459,8 +461,3 @@ def attention_copied(q, k, v, offsets, peers: PeerOutputs, *, rank: int, world: 
         timing["tail"] = (tail_start, event())
     return peers.out
 
-
-def ctypes_void_p(value: int):
-    import ctypes
-
-    return ctypes.c_void_p(value)
