@@ -298,20 +298,27 @@ class PeerOutputs:
     IPC handles (abx_ipc_handle) over the process group and map the others'
     copies for this rank's device (abx_ipc_open, peer access enabled), so one
     kernel can store its rows into all of them over NVLink. `pointers` lists the
-    device addresses in rank order (this rank's own copy at its rank). Call
-    `close()` before the process group is destroyed.
+    device addresses in rank order (this rank's own copy at its rank).
+    `copy_streams` (1 to world - 1) are the streams `attention_copied` pushes
+    finished head blocks on; peers are spread over them, so with world - 1
+    streams every peer's copy runs on its own stream. Call `close()` before the
+    process group is destroyed.
     """
 
-    def __init__(self, out: torch.Tensor, group=None):
+    def __init__(self, out: torch.Tensor, group=None, copy_streams: int = 1):
         import torch.distributed as dist
 
         from . import _lib
 
         self.out = out
         self._lib = _lib.load()
-        self.copy_stream = torch.cuda.Stream(out.device)  # peer copies of finished head blocks
         world = dist.get_world_size(group)
         rank = dist.get_rank(group)
+        if not 1 <= copy_streams <= max(1, world - 1):
+            raise ValueError(f"copy_streams must be in [1, {max(1, world - 1)}], got {copy_streams}")
+        # peer copies of finished head blocks
+        self.copy_streams = [torch.cuda.Stream(out.device) for _ in range(copy_streams)]
+        self.copy_stream = self.copy_streams[0]
         handle = ctypes.create_string_buffer(64)
         offset = ctypes.c_size_t(0)
         with torch.cuda.device(out.device):
@@ -395,11 +402,14 @@ def attention_copied(q, k, v, offsets, peers: PeerOutputs, *, rank: int, world: 
 
     Same block-interleaved heads and plan as `attention_sharded`; each block's
     prefill writes its rows straight into this rank's copy of the layer output
-    (at the block's global heads), and as soon as it finishes, a copy stream
-    pushes that slice into every other rank's copy (`abx_peer_copy` through the
+    (at the block's global heads), and as soon as it finishes, the copy streams
+    push that slice into every other rank's copy (`abx_peer_copy` through the
     `peers` mappings: copy engines over NVLink, no SMs), so the next block's
-    prefill keeps every SM. Two one-element all-reduces bracket the step, as in
-    `attention_scatter`. Returns when `peers.out` is complete on the current stream.
+    prefill keeps every SM. Rank g visits its peers in the order g + 1, g + 2, ...
+    (mod world), dealt round-robin over `peers.copy_streams`, so the ranks start
+    on different destinations. Two one-element all-reduces bracket the step, as
+    in `attention_scatter`. Returns when `peers.out` is complete on the current
+    stream.
     """
     import torch.distributed as dist
 
@@ -413,7 +423,8 @@ def attention_copied(q, k, v, offsets, peers: PeerOutputs, *, rank: int, world: 
     head_bytes = tokens * dim * q.element_size()
     lib = _lib.load()
     main = torch.cuda.current_stream(q.device)
-    copy = peers.copy_stream
+    streams = peers.copy_streams
+    targets = [(rank + i) % world for i in range(1, world)]
     own = peers.pointers[rank]
     flag = torch.zeros(1, dtype=torch.float32, device=q.device)
 
@@ -446,16 +457,18 @@ def attention_copied(q, k, v, offsets, peers: PeerOutputs, *, rank: int, world: 
         done = event()
         if timing is not None:
             timing["blocks"].append((start, done))
-        copy.wait_event(done)
-        for r, ptr in enumerate(peers.pointers):
-            if r != rank:
-                _lib.check(lib.abx_peer_copy(ctypes.c_void_p(ptr + head0 * head_bytes),
-                                             ctypes.c_void_p(own + head0 * head_bytes), b * head_bytes,
-                                             ctypes.c_void_p(copy.cuda_stream)), "abx_peer_copy")
+        for s in streams:
+            s.wait_event(done)
+        for i, r in enumerate(targets):
+            s = streams[i % len(streams)]
+            _lib.check(lib.abx_peer_copy(ctypes.c_void_p(peers.pointers[r] + head0 * head_bytes),
+                                         ctypes.c_void_p(own + head0 * head_bytes), b * head_bytes,
+                                         ctypes.c_void_p(s.cuda_stream)), "abx_peer_copy")
         first += world * b
         local += b
     tail_start = event() if timing is not None else None
-    main.wait_stream(copy)
+    for s in streams:
+        main.wait_stream(s)
     dist.all_reduce(flag, group=group)  # every rank's rows have landed in every copy
     if timing is not None:
         timing["tail"] = (tail_start, event())

@@ -356,6 +356,9 @@ def main() -> None:
                         help="N > 1: reassemble the output with NCCL all-gathers of head blocks, with copy-engine "
                              "peer copies of each finished block (copy), or have the prefill store every row "
                              "into all ranks' copies over NVLink (peer)")
+    parser.add_argument("--copy-streams", type=int, default=1,
+                        help="N > 1 with --gather copy: streams the peer copies of a block are spread over "
+                             "(1 .. N - 1)")
     parser.add_argument("--nccl-priority", default="normal", choices=["normal", "high"],
                         help="N > 1: priority of NCCL's stream")
     parser.add_argument("--no-ref-kernels", action="store_true",
@@ -433,7 +436,8 @@ def main() -> None:
     tokens = shape.tokens
     offsets = shard.shard_offsets(shard.layer_offsets(bh, tokens, shape.seed, device), tokens, heads)
     gathered = torch.empty((bh, tokens, 128), dtype=torch.bfloat16, device=device) if world > 1 else None
-    peers = shard.PeerOutputs(gathered) if world > 1 and args.gather in ("peer", "copy") else None
+    peers = (shard.PeerOutputs(gathered, copy_streams=args.copy_streams if args.gather == "copy" else 1)
+             if world > 1 and args.gather in ("peer", "copy") else None)
 
     def sharded_step(qq, kk, vv, timing=None):
         if args.gather == "copy":
@@ -604,7 +608,8 @@ def main() -> None:
                               " with every output row stored into all ranks' copies by the prefill (peer stores)"
                               if args.gather == "peer" else
                               f" in head blocks of {chunks} heads per rank, each copied to every rank by copy "
-                              f"engines while the next computes" if args.gather == "copy" else
+                              f"engines ({args.copy_streams} stream(s)) while the next computes"
+                              if args.gather == "copy" else
                               f" in head blocks of {chunks} heads per rank, each all-gathered while the next "
                               f"computes")},
         "eff_tflops": eq_flops / (ms * 1e-3) / 1e12,

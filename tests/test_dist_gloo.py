@@ -190,3 +190,27 @@ def _uneven_worker(rank, world, port, result_path, sizes):
             torch.save({"status": "ok", "full": out}, result_path)
     finally:
         dist.destroy_process_group()
+
+
+def _copy_streams_worker(rank, world, port, result_path, count):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=timedelta(seconds=10))
+    try:
+        try:
+            shard.PeerOutputs(torch.empty(4, 8), copy_streams=count)
+            status = "accepted"
+        except ValueError:
+            status = "ValueError"
+        if rank == 0:
+            torch.save({"status": status}, result_path)
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("count", [0, 2])
+def test_peer_outputs_rejects_copy_stream_counts_outside_one_to_world_minus_one(tmp_path, count):
+    # With 2 ranks a block has one peer to copy to: one copy stream at most.
+    path = str(tmp_path / "out.pt")
+    mp.start_processes(_copy_streams_worker, args=(2, _free_port(), path, count), nprocs=2, join=True,
+                       start_method="spawn")
+    assert torch.load(path)["status"] == "ValueError"
