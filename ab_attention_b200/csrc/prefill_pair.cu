@@ -34,14 +34,20 @@
 //              S_g = Q_g K^T into the group's S/P columns, O_g += P_g V with P
 //              read from TMEM; per group PV(k) then S(k + 1), groups interleaved,
 //              so one group's PV and S run while the other group's softmax runs.
+//              V(k) and K(k + 1) are waited for before P(k), so both products
+//              follow the softmax's hand-over back to back.
 //   warps 9-11 K gathers (and Q), warps 12-15 V gathers: one TMA box of 4 rows
 //              x 64 columns per lane, 128-byte swizzled into the UMMA tile.
-// A softmax thread reads its whole 128-column S row from TMEM in one go (four
+// A softmax thread takes its tile's 32 granule weights (warp shuffles) while S is
+// being computed, reads its whole 128-column S row from TMEM in one go (four
 // loads, one wait), takes the row max and the exponentials in registers and
 // writes P back with four stores: two TMEM round trips per tile.
 // TMEM: O_A [0,128), O_B [128,256), S/P of A [256,384), of B [384,512).
 // Shared memory: Q_A, Q_B (64 KB), three K and two V stages of 32 KB.
-// Every wait is bounded as in prefill.cu.
+// Every wait is bounded as in prefill.cu, and lets the hardware suspend the
+// waiting warp (mbarrier try_wait without a time hint): each sub-partition holds
+// one warp of each softmax group beside the MMA or gather warps, and a polling
+// warp would take issue slots from the one that is computing.
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
@@ -400,6 +406,7 @@ __device__ __forceinline__ void mask_tail(uint32_t s_col, int local, int tail) {
     tc::tmem_wait_st();
 }
 
+
 __global__ void __launch_bounds__(kThreads, 1) prefill_pair_kernel(const PairArgs args,
                                                                    const __grid_constant__ PairMaps maps) {
     extern __shared__ uint8_t smem_raw[];
@@ -502,7 +509,7 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_pair_kernel(const PairArg
             code_cur = code_next;
             if (j + 2 < stream_tiles) code_next = __ldg(codes + (j + 2) * kTileGranules);
             const bool free_ok =
-                use == 0 || tc::mbar_wait(bar(bar_empty + st), (use - 1) & 1, abort_flag, kWaitLimit);
+                use == 0 || tc::mbar_wait_suspend(bar(bar_empty + st), (use - 1) & 1, abort_flag, kWaitLimit);
             if (!__all_sync(0xffffffffu, free_ok)) break;
             issued = j + 1;
             if (lane == 0) tc::mbar_arrive_expect_tx(bar(bar_full + st), warp_boxes * kBoxBytes);
@@ -514,23 +521,27 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_pair_kernel(const PairArg
         if (lane == 0) {
             for (int st = 0; st < stages && st < issued; ++st) {
                 const int last_use = (issued - 1 - st) / stages;
-                tc::mbar_wait(bar(bar_full + st), last_use & 1, abort_flag, kWaitLimit, /*honor_abort=*/false);
+                tc::mbar_wait_suspend(bar(bar_full + st), last_use & 1, abort_flag, kWaitLimit,
+                                      /*honor_abort=*/false);
             }
-            if (warp == kKLoadWarp) tc::mbar_wait(bar(kBarQFull), 0, abort_flag, kWaitLimit, /*honor_abort=*/false);
+            if (warp == kKLoadWarp)
+                tc::mbar_wait_suspend(bar(kBarQFull), 0, abort_flag, kWaitLimit, /*honor_abort=*/false);
         }
         __syncwarp();
     } else if (warp == kMmaWarp) {
         // ---- MMA issue: per group PV(k) then S(k + 1); A's, then B's; stream order -------------
         // The whole warp runs this loop (warp-uniform operands); one elected lane issues.
         {
-            bool ok = tc::mbar_wait_warp(bar(kBarQFull), 0, abort_flag, kWaitLimit);
+            bool ok = tc::mbar_wait_warp_suspend(bar(kBarQFull), 0, abort_flag, kWaitLimit);
             // A shared tile is read by A, then B; its stages are released after B's MMA.
             auto last_reader = [&](int j, int g) { return j >= inf.x || g == 1 || !has_b; };
-            auto issue_s = [&](int g, int k) -> bool {
-                const int j = stream_tile(inf, g, k);
+            auto k_ready = [&](int j) {
+                return tc::mbar_wait_warp_suspend(bar(kBarKFull + j % kKStages), (j / kKStages) & 1, abort_flag,
+                                                  kWaitLimit);
+            };
+            // S_g = Q_g K^T of stream tile j into the group's S/P columns (its K stage resident).
+            auto issue_s = [&](int g, int j) {
                 const int st = j % kKStages;
-                if (!tc::mbar_wait_warp(bar(kBarKFull + st), (j / kKStages) & 1, abort_flag, kWaitLimit)) return false;
-                tc::fence_after_sync();
                 const uint64_t adesc0 = tc::smem_desc(base + kOffQ + g * kQBytes, 16, 1024, tc::kSwizzle128B);
                 const uint64_t bdesc0 = tc::smem_desc(base + kOffK + st * kTileBytes, 16, 1024, tc::kSwizzle128B);
 #pragma unroll
@@ -542,13 +553,18 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_pair_kernel(const PairArg
                 }
                 tc::mma_commit_elect(bar(kBarSFull + g));
                 if (last_reader(j, g)) tc::mma_commit_elect(bar(kBarKEmpty + st));
-                return true;
             };
-            auto issue_pv = [&](int g, int k) -> bool {
+            // Step k of group g: PV(k), then S(k + 1). V(k) and K(k + 1) are waited for
+            // before P(k), so once the softmax hands over P both go out back to back.
+            auto step = [&](int g, int k) -> bool {
                 const int j = stream_tile(inf, g, k);
                 const int st = j % kVStages;
-                if (!tc::mbar_wait_warp(bar(kBarVFull + st), (j / kVStages) & 1, abort_flag, kWaitLimit)) return false;
-                if (!tc::mbar_wait_warp(bar(kBarPFull + g), k & 1, abort_flag, kWaitLimit)) return false;
+                const bool next = k + 1 < tiles_of(g);
+                const int jn = next ? stream_tile(inf, g, k + 1) : 0;
+                if (!tc::mbar_wait_warp_suspend(bar(kBarVFull + st), (j / kVStages) & 1, abort_flag, kWaitLimit))
+                    return false;
+                if (next && !k_ready(jn)) return false;
+                if (!tc::mbar_wait_warp_suspend(bar(kBarPFull + g), k & 1, abort_flag, kWaitLimit)) return false;
                 tc::fence_after_sync();
                 const uint64_t bdesc0 =
                     tc::smem_desc(base + kOffV + st * kTileBytes, kSlabBytes, 1024, tc::kSwizzle128B);
@@ -561,21 +577,29 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_pair_kernel(const PairArg
                 }
                 if (last_reader(j, g)) tc::mma_commit_elect(bar(kBarVEmpty + st));
                 if (k + 1 == tiles_of(g)) tc::mma_commit_elect(bar(kBarOFinal + g));
+                // S(k + 1) overwrites the group's S/P columns: it follows PV(k) in the pipe.
+                if (next) issue_s(g, jn);
                 return true;
             };
-            for (int g = 0; ok && g < kGroups; ++g)
-                if (tiles_of(g) > 0 && !issue_s(g, 0)) ok = false;
+            for (int g = 0; ok && g < kGroups; ++g) {
+                if (tiles_of(g) == 0) continue;
+                const int j0 = stream_tile(inf, g, 0);
+                if (!k_ready(j0)) {
+                    ok = false;
+                    break;
+                }
+                tc::fence_after_sync();
+                issue_s(g, j0);
+            }
             const int steps = max(tiles_of(0), tiles_of(1));
             for (int k = 0; ok && k < steps; ++k) {
                 for (int g = 0; ok && g < kGroups; ++g) {
                     if (k >= tiles_of(g)) continue;
-                    if (!issue_pv(g, k)) ok = false;
-                    // S(k + 1) overwrites the group's S/P columns: it follows PV(k) in the pipe.
-                    else if (k + 1 < tiles_of(g) && !issue_s(g, k + 1)) ok = false;
+                    if (!step(g, k)) ok = false;
                 }
             }
             tc::mma_commit_elect(bar(kBarDrain));
-            if (lane == 0) tc::mbar_wait(bar(kBarDrain), 0, abort_flag, kWaitLimit, /*honor_abort=*/false);
+            if (lane == 0) tc::mbar_wait_suspend(bar(kBarDrain), 0, abort_flag, kWaitLimit, /*honor_abort=*/false);
         }
         __syncwarp();
     }
@@ -603,7 +627,14 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_pair_kernel(const PairArg
             const float w_lane = w_next;
             if (k + 1 < tiles) w_next = entry_weight(args, row_g, g, entry_next);
             if (k + 2 < tiles) entry_next = __ldg(entries + stream_tile(inf, g, k + 2) * kTileGranules + wl);
-            if (!tc::mbar_wait_warp(bar(kBarSFull + g), k & 1, abort_flag, kWaitLimit)) {
+            // The tile's 32 granule weights in every lane, taken while S is still being computed.
+            float wv[kTileGranules];
+#pragma unroll
+            for (int gi = 0; gi < kTileGranules; ++gi) {
+                wv[gi] = __shfl_sync(0xffffffffu, w_lane, gi);
+                asm volatile("" : "+f"(wv[gi]));
+            }
+            if (!tc::mbar_wait_warp_suspend(bar(kBarSFull + g), k & 1, abort_flag, kWaitLimit)) {
                 ok = false;
                 break;
             }
@@ -631,12 +662,10 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_pair_kernel(const PairArg
             }
             // Row max of x = s * kappa + w (per granule: fma(max s, kappa, w)); the
             // granule weights stay in registers for the exponentials.
-            float wv[kTileGranules];
             float part_max[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
 #pragma unroll
             for (int gi = 0; gi < kTileGranules; ++gi) {
-                const float w = __shfl_sync(0xffffffffu, w_lane, gi);
-                wv[gi] = w;
+                const float w = wv[gi];
                 const float smax = max3f(__uint_as_float(col(4 * gi)), __uint_as_float(col(4 * gi + 1)),
                                          fmaxf(__uint_as_float(col(4 * gi + 2)), __uint_as_float(col(4 * gi + 3))));
                 part_max[gi & 3] = fmaxf(part_max[gi & 3], fmaf(smax, args.kappa, w));
@@ -697,7 +726,7 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_pair_kernel(const PairArg
             tc::fence_before_sync();
             tc::mbar_arrive(bar(kBarPFull + g));
         }
-        if (ok && tiles > 0 && tc::mbar_wait_warp(bar(kBarOFinal + g), 0, abort_flag, kWaitLimit)) {
+        if (ok && tiles > 0 && tc::mbar_wait_warp_suspend(bar(kBarOFinal + g), 0, abort_flag, kWaitLimit)) {
             // o = O / l, lse = m + log2(l) for this block's rows.
             tc::fence_after_sync();
             const int64_t token0 = (block_a + g) * kQueryBlock;

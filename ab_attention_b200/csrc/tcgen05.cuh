@@ -76,6 +76,44 @@ __device__ __forceinline__ bool mbar_wait_warp(uint32_t bar, uint32_t parity, vo
     return __all_sync(0xffffffffu, ok);
 }
 
+// The same waits with hardware suspension: try_wait without a time hint lets the
+// hardware suspend the thread until the phase completes (or a system-dependent
+// time passes), so a waiting warp takes no issue slots from the warps sharing its
+// sub-partition. Bounded like mbar_wait (the clock and the abort flag are checked
+// every 16 polls, each of which may suspend).
+__device__ __forceinline__ bool mbar_try_wait_suspend(uint32_t bar, uint32_t parity) {
+    uint32_t done;
+    asm volatile(
+        "{\n"
+        ".reg .pred p;\n"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n"
+        "selp.u32 %0, 1, 0, p;\n"
+        "}\n"
+        : "=r"(done)
+        : "r"(bar), "r"(parity)
+        : "memory");
+    return done != 0;
+}
+__device__ __forceinline__ bool mbar_wait_suspend(uint32_t bar, uint32_t parity, volatile int* abort,
+                                                  uint64_t limit_cycles, bool honor_abort = true) {
+    if (mbar_try_wait_suspend(bar, parity)) return true;
+    const long long start = clock64();
+    for (uint32_t spin = 1; spin < (1u << 28); ++spin) {
+        if (mbar_try_wait_suspend(bar, parity)) return true;
+        if ((spin & 15) == 0) {
+            if (honor_abort && *abort) return false;
+            if (static_cast<uint64_t>(clock64() - start) > limit_cycles) break;
+        }
+    }
+    *abort = 1;
+    return false;
+}
+__device__ __forceinline__ bool mbar_wait_warp_suspend(uint32_t bar, uint32_t parity, volatile int* abort,
+                                                       uint64_t limit_cycles) {
+    const bool ok = mbar_wait_suspend(bar, parity, abort, limit_cycles);
+    return __all_sync(0xffffffffu, ok);
+}
+
 // ---- proxies and TMEM ordering -------------------------------------------------------
 
 __device__ __forceinline__ void fence_proxy_async_smem() {

@@ -122,9 +122,9 @@ class ClockSampler:
 
 # DRAM bytes (read + write) of one paired prefill launch per head at the Wan shape,
 # from one ncu capture of the 4-head case (dram__bytes_read.sum + dram__bytes_write.sum
-# = 279.82 + 63.76 MB; its 232 MB of Q/K/V exceed L2); a head's K/V stay L2-resident
+# = 278.78 + 61.46 MB; its 232 MB of Q/K/V exceed L2); a head's K/V stay L2-resident
 # while its pairs run, so traffic scales with heads.
-PREFILL_DRAM_BYTES_PER_HEAD = (279.82e6 + 63.76e6) / 4
+PREFILL_DRAM_BYTES_PER_HEAD = (278.78e6 + 61.46e6) / 4
 
 
 def plan_bytes(bh: int, tokens: int, samples: int) -> float:
