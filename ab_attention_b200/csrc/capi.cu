@@ -24,20 +24,27 @@ int* device_error_word() {
     return static_cast<int*>(ptr);
 }
 
-// One warp waits, bounded by limit_cycles, on an mbarrier that nothing arrives
-// at: the library's bounded wait gives up and the kernel records
-// ABX_ERR_DEVICE_TIMEOUT, exercising the timeout path without a fault.
+// Two warps wait, bounded by limit_cycles, on an mbarrier that nothing arrives
+// at: warp 0 with the library's polling wait, warp 1 with its suspending wait
+// (the form the prefill kernels use). Both give up, each on its own abort flag,
+// and the kernel records ABX_ERR_DEVICE_TIMEOUT only when both did, exercising
+// both timeout paths without a fault.
 __global__ void wait_selftest_kernel(uint64_t limit_cycles, int* error) {
     __shared__ __align__(8) uint64_t bar;
-    __shared__ int abort_flag;
+    __shared__ int abort_flag[2];
+    __shared__ int gave_up[2];
+    const int w = threadIdx.x >> 5;
     if (threadIdx.x == 0) {
-        abort_flag = 0;
+        abort_flag[0] = abort_flag[1] = 0;
         tc::mbar_init(smem_addr(&bar), 1);
         tc::mbar_init_fence();
     }
-    __syncwarp();
-    const bool ok = tc::mbar_wait_warp(smem_addr(&bar), 0, &abort_flag, limit_cycles);
-    if (!ok && threadIdx.x == 0) raise_device_error(error, ABX_ERR_DEVICE_TIMEOUT);
+    __syncthreads();
+    const bool ok = w == 0 ? tc::mbar_wait_warp(smem_addr(&bar), 0, &abort_flag[0], limit_cycles)
+                           : tc::mbar_wait_warp_suspend(smem_addr(&bar), 0, &abort_flag[1], limit_cycles);
+    if ((threadIdx.x & 31) == 0) gave_up[w] = !ok;
+    __syncthreads();
+    if (threadIdx.x == 0 && gave_up[0] && gave_up[1]) raise_device_error(error, ABX_ERR_DEVICE_TIMEOUT);
 }
 
 }  // namespace abx
@@ -630,7 +637,7 @@ int abx_cross_prefill(const void* q, int64_t q_tokens, const void* k, const void
 int abx_selftest_wait_timeout(int64_t limit_cycles, abx_stream_t stream) {
     if (limit_cycles <= 0 || limit_cycles > 4000000000LL)
         return fail(ABX_ERR_INVALID_ARGUMENT, "limit must be in (0, 4e9] cycles");
-    abx::wait_selftest_kernel<<<1, 32, 0, stream>>>(static_cast<uint64_t>(limit_cycles), abx::device_error_word());
+    abx::wait_selftest_kernel<<<1, 64, 0, stream>>>(static_cast<uint64_t>(limit_cycles), abx::device_error_word());
     return check_cuda(cudaGetLastError(), "self-test launch");
 }
 

@@ -38,6 +38,8 @@
 // (checked at compile time and against the kernel's attributes on the host).
 // Every mbarrier wait is bounded; on expiry the CTA drains its copies and MMAs,
 // frees TMEM, records ABX_ERR_DEVICE_TIMEOUT in the device error word and exits.
+// The waits let the hardware suspend the waiting warp (try_wait without a time
+// hint), so it takes no issue slots from the warps computing beside it.
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
@@ -293,7 +295,7 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const PrefillArgs 
             const int id = next_id;
             if (t + 1 < tiles) next_id = granule_id(args, row_ids, slot + kTileGranules);
             const bool free_ok =
-                use == 0 || tc::mbar_wait(bar(bar_empty + st), (use - 1) & 1, abort_flag, kWaitLimit);
+                use == 0 || tc::mbar_wait_suspend(bar(bar_empty + st), (use - 1) & 1, abort_flag, kWaitLimit);
             if (!__all_sync(0xffffffffu, free_ok)) break;
             issued = t + 1;
             if (row_ids == nullptr && (t + 1) * kTileGranules <= args.samples) {
@@ -325,22 +327,25 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const PrefillArgs 
         if (lane == 0) {
             for (int st = 0; st < stages && st < issued; ++st) {
                 const int last_use = (issued - 1 - st) / stages;
-                tc::mbar_wait(bar(bar_full + st), last_use & 1, abort_flag, kWaitLimit, /*honor_abort=*/false);
+                tc::mbar_wait_suspend(bar(bar_full + st), last_use & 1, abort_flag, kWaitLimit,
+                                      /*honor_abort=*/false);
             }
-            if (warp == kKLoadWarp) tc::mbar_wait(bar(kBarQFull), 0, abort_flag, kWaitLimit, /*honor_abort=*/false);
+            if (warp == kKLoadWarp)
+                tc::mbar_wait_suspend(bar(kBarQFull), 0, abort_flag, kWaitLimit, /*honor_abort=*/false);
         }
         __syncwarp();
     } else if (warp == kMmaWarp) {
         // ---- MMA issue ------------------------------------------------------------------------
         // The whole warp runs this loop (warp-uniform operands); one elected lane issues.
         {
-            bool ok = tc::mbar_wait_warp(bar(kBarQFull), 0, abort_flag, kWaitLimit);
+            bool ok = tc::mbar_wait_warp_suspend(bar(kBarQFull), 0, abort_flag, kWaitLimit);
             const uint64_t qdesc0 = tc::smem_desc(base + kOffQ, 16, 1024, tc::kSwizzle128B);
             auto issue_pv = [&](int u) -> bool {
                 const int b = u & 1;
                 const int vst = u % kVStages;
-                if (!tc::mbar_wait_warp(bar(kBarVFull + vst), (u / kVStages) & 1, abort_flag, kWaitLimit)) return false;
-                if (!tc::mbar_wait_warp(bar(kBarPFull + b), (u >> 1) & 1, abort_flag, kWaitLimit)) return false;
+                if (!tc::mbar_wait_warp_suspend(bar(kBarVFull + vst), (u / kVStages) & 1, abort_flag, kWaitLimit))
+                    return false;
+                if (!tc::mbar_wait_warp_suspend(bar(kBarPFull + b), (u >> 1) & 1, abort_flag, kWaitLimit)) return false;
                 tc::fence_after_sync();
                 const uint64_t vdesc0 =
                     tc::smem_desc(base + kOffV + vst * kTileBytes, kSlabBytes, 1024, tc::kSwizzle128B);
@@ -359,7 +364,7 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const PrefillArgs 
             for (int t = 0; ok && t < tiles; ++t) {
                 const int b = t & 1;
                 const int kst = t % kKStages;
-                if (!tc::mbar_wait_warp(bar(kBarKFull + kst), (t / kKStages) & 1, abort_flag, kWaitLimit)) {
+                if (!tc::mbar_wait_warp_suspend(bar(kBarKFull + kst), (t / kKStages) & 1, abort_flag, kWaitLimit)) {
                     ok = false;
                     break;
                 }
@@ -378,7 +383,7 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const PrefillArgs 
             if (ok) tc::mma_commit_elect(bar(kBarOFinal));
             // Drain: every MMA issued above has completed before TMEM is freed.
             tc::mma_commit_elect(bar(kBarDrain));
-            if (lane == 0) tc::mbar_wait(bar(kBarDrain), 0, abort_flag, kWaitLimit, /*honor_abort=*/false);
+            if (lane == 0) tc::mbar_wait_suspend(bar(kBarDrain), 0, abort_flag, kWaitLimit, /*honor_abort=*/false);
         }
         __syncwarp();
     }
@@ -402,7 +407,7 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const PrefillArgs 
             const float w_lane = w_next;
             if (t + kSoftmaxGroups < tiles)
                 w_next = slot_weight(args, row_w, (t + kSoftmaxGroups) * kTileGranules + lane);
-            if (!tc::mbar_wait_warp(bar(kBarSFull + g), (t >> 1) & 1, abort_flag, kWaitLimit)) {
+            if (!tc::mbar_wait_warp_suspend(bar(kBarSFull + g), (t >> 1) & 1, abort_flag, kWaitLimit)) {
                 ok = false;
                 break;
             }
@@ -510,8 +515,8 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const PrefillArgs 
             merge_m[r] = m_used;
             merge_l[r] = l_sum;
             tc::mbar_arrive(bar(kBarMerge));
-        } else if (ok && tc::mbar_wait_warp(bar(kBarOFinal), 0, abort_flag, kWaitLimit) &&
-                   tc::mbar_wait_warp(bar(kBarMerge), 0, abort_flag, kWaitLimit)) {
+        } else if (ok && tc::mbar_wait_warp_suspend(bar(kBarOFinal), 0, abort_flag, kWaitLimit) &&
+                   tc::mbar_wait_warp_suspend(bar(kBarMerge), 0, abort_flag, kWaitLimit)) {
             // Merge the two partial softmaxes: o = (O0 2^(m0-m) + O1 2^(m1-m)) / (l0 2^(m0-m) + l1 2^(m1-m)).
             tc::fence_after_sync();
             const float m1 = merge_m[r];

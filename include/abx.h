@@ -47,8 +47,9 @@ const char* abx_last_error(void);
 int abx_device_status(abx_stream_t stream, int clear, int* status_out);
 
 /* Self-test of the device-side failure path (no counterpart in the reference):
- * one warp waits, bounded by limit_cycles SM clock cycles, on an mbarrier that
- * nothing arrives at; the wait gives up, the kernel returns normally and the
+ * two warps wait, bounded by limit_cycles SM clock cycles, on an mbarrier that
+ * nothing arrives at, one with the polling and one with the suspending form of
+ * the library's bounded wait; both give up, the kernel returns normally and the
  * device error word reads ABX_ERR_DEVICE_TIMEOUT. The context stays usable. */
 int abx_selftest_wait_timeout(int64_t limit_cycles, abx_stream_t stream);
 
