@@ -406,7 +406,6 @@ __device__ __forceinline__ void mask_tail(uint32_t s_col, int local, int tail) {
     tc::tmem_wait_st();
 }
 
-
 __global__ void __launch_bounds__(kThreads, 1) prefill_pair_kernel(const PairArgs args,
                                                                    const __grid_constant__ PairMaps maps) {
     extern __shared__ uint8_t smem_raw[];
